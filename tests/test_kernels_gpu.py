@@ -1,0 +1,316 @@
+"""Parity of the sm_100a kernels with the CPU oracle, through the C-ABI.
+
+Bounds (the reference CPU backend is the oracle, oracle/oracle.c):
+  relu / add / multiply / transpose / split copies: bit-exact
+  sigmoid: <= 2 ulp
+  reductions: <= 1e-5 relative to the fp64 sum of the oracle's own
+              element-wise values (the CPU's sequential fp32 sum is itself
+              ~1e-4 off at 1e6 terms)
+  matmul: norm-wise relative error <= 1e-5 (FFMA path), <= 2e-3 (TF32 path)
+"""
+import numpy as np
+import pytest
+
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+RTOL_REDUCE = 1e-5
+RTOL_FFMA = 1e-5
+RTOL_TF32 = 2e-3
+
+
+def ulp_dist(a, b):
+    a = np.ascontiguousarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.ascontiguousarray(b, np.float32).view(np.int32).astype(np.int64)
+    a = np.where(a < 0, -(a & 0x7FFFFFFF), a)
+    b = np.where(b < 0, -(b & 0x7FFFFFFF), b)
+    return np.abs(a - b)
+
+
+def normwise(got, want):
+    want64 = want.astype(np.float64)
+    return np.linalg.norm(got.astype(np.float64) - want64) / max(np.linalg.norm(want64), 1e-300)
+
+
+def dev(ttc, a):
+    return ttc.DeviceArray.from_numpy(a)
+
+
+def run_unary(ttc, op, x):
+    X = dev(ttc, x)
+    Y = ttc.DeviceArray.empty(x.shape)
+    rows = x.shape[0] if x.ndim > 1 else 1
+    cols = x.size // rows
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(op), ttc.instr(ttc.OP_STORE, idx=0)]
+    ttc.eltwise_chain(ttc.chain_desc(rows, cols, [ttc.in_view(X.ptr, cols)], [ttc.out_view(Y.ptr, cols)], prog))
+    return Y.numpy()
+
+
+SHAPES = [(1, 1), (1, 7), (3, 5), (64, 64), (1000, 1000), (17, 1028), (4099, 3)]
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+def test_relu_bit_exact(ttc, shape):
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, shape).astype(np.float32)
+    x.flat[0] = -0.0
+    if x.size > 2:
+        x.flat[1] = np.nan
+        x.flat[2] = np.float32(1e-45)
+    got = run_unary(ttc, ttc.OP_RELU, x)
+    assert np.array_equal(got.view(np.int32), oracle.relu(x).view(np.int32))
+
+
+def test_sigmoid_within_2ulp(ttc, golden):
+    got = run_unary(ttc, ttc.OP_SIGMOID, golden["sig_x"].reshape(1, -1))
+    assert ulp_dist(got.ravel(), golden["sig_y"]).max() <= 2
+    rng = np.random.default_rng(1)
+    x = rng.uniform(-30, 30, (2048, 2048)).astype(np.float32)
+    got = run_unary(ttc, ttc.OP_SIGMOID, x)
+    d = ulp_dist(got, oracle.sigmoid(x))
+    assert d.max() <= 2, d.max()
+
+
+@pytest.mark.parametrize("shape", SHAPES)
+@pytest.mark.parametrize("op", ["add", "mul"])
+def test_binary_bit_exact(ttc, shape, op):
+    rng = np.random.default_rng(2)
+    a = rng.uniform(-1, 1, shape).astype(np.float32)
+    b = rng.uniform(-1, 1, shape).astype(np.float32)
+    A, B = dev(ttc, a), dev(ttc, b)
+    Y = ttc.DeviceArray.empty(shape)
+    rows, cols = shape
+    code = ttc.OP_ADD if op == "add" else ttc.OP_MUL
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(code, ttc.SRC_INPUT, 1), ttc.instr(ttc.OP_STORE, idx=0)]
+    ttc.eltwise_chain(ttc.chain_desc(rows, cols, [ttc.in_view(A.ptr, cols), ttc.in_view(B.ptr, cols)],
+                                     [ttc.out_view(Y.ptr, cols)], prog))
+    want = oracle.add(a, b) if op == "add" else oracle.multiply(a, b)
+    assert np.array_equal(Y.numpy(), want)
+
+
+@pytest.mark.parametrize("shape", [(37, 64), (256, 1024), (5, 3), (300, 17)])
+def test_bias_add_broadcast(ttc, shape, golden):
+    rng = np.random.default_rng(3)
+    a = rng.uniform(-1, 1, shape).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, (1, shape[1])).astype(np.float32)
+    A, Bb = dev(ttc, a), dev(ttc, bias)
+    Y = ttc.DeviceArray.empty(shape)
+    rows, cols = shape
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(ttc.OP_ADD, ttc.SRC_INPUT, 1), ttc.instr(ttc.OP_STORE, idx=0)]
+    ttc.eltwise_chain(ttc.chain_desc(rows, cols, [ttc.in_view(A.ptr, cols), ttc.in_view(Bb.ptr, 0)],
+                                     [ttc.out_view(Y.ptr, cols)], prog))
+    assert np.array_equal(Y.numpy(), oracle.add(a, bias))
+
+
+def test_readme_chain_fused_with_sum(ttc, golden):
+    """w = multiply(add(relu(x), relu(x)), ...) and s = reduce_sum(w) in one kernel
+    (the README chain, x[1000,1000] ~ U(-1,1))."""
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, (1000, 1000)).astype(np.float32)
+    X = dev(ttc, x)
+    W = ttc.DeviceArray.empty(x.shape)
+    S = ttc.DeviceArray.empty((1,))
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(ttc.OP_RELU), ttc.instr(ttc.OP_ADD, ttc.SRC_ACC),
+            ttc.instr(ttc.OP_MUL, ttc.SRC_ACC), ttc.instr(ttc.OP_STORE, idx=0)]
+    ttc.eltwise_chain(ttc.chain_desc(1000, 1000, [ttc.in_view(X.ptr, 1000)], [ttc.out_view(W.ptr, 1000)], prog,
+                                     reduce=ttc.REDUCE_ALL, reduce_out=S.ptr))
+    y = oracle.relu(x)
+    z = oracle.add(y, y)
+    w = oracle.multiply(z, z)
+    assert np.array_equal(W.numpy(), w)
+    exact = oracle.reduce(w, f64=True)[0]
+    s = S.numpy()[0]
+    assert abs(s - exact) <= RTOL_REDUCE * abs(exact)
+    # golden fixture of the lazy path (reference tape executor)
+    c = golden["chain_x"]
+    C_, Wc = dev(ttc, c), ttc.DeviceArray.empty(c.shape)
+    ttc.eltwise_chain(ttc.chain_desc(c.shape[0], c.shape[1], [ttc.in_view(C_.ptr, c.shape[1])],
+                                     [ttc.out_view(Wc.ptr, c.shape[1])], prog))
+    assert np.array_equal(Wc.numpy(), golden["chain_w"])
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (3, 5), (1000, 1000), (19, 300), (65, 4096), (4096, 20), (7, 2051)])
+@pytest.mark.parametrize("mode", ["rows", "cols", "all"])
+@pytest.mark.parametrize("mean", [False, True])
+def test_chain_reductions(ttc, shape, mode, mean):
+    rng = np.random.default_rng(4)
+    x = rng.uniform(-1, 1, shape).astype(np.float32)
+    X = dev(ttc, x)
+    rows, cols = shape
+    n_out = {"rows": rows, "cols": cols, "all": 1}[mode]
+    red = {"rows": ttc.REDUCE_ROWS, "cols": ttc.REDUCE_COLS, "all": ttc.REDUCE_ALL}[mode]
+    dims = {"rows": (1,), "cols": (0,), "all": ()}[mode]
+    O = ttc.DeviceArray.empty((n_out,))
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(ttc.OP_SIGMOID)]
+    ttc.eltwise_chain(ttc.chain_desc(rows, cols, [ttc.in_view(X.ptr, cols)], [], prog, reduce=red,
+                                     reduce_out=O.ptr, mean=mean))
+    sig = oracle.sigmoid(x)
+    want = oracle.reduce(sig, dims, mean=mean, f64=True).ravel()
+    got = O.numpy()
+    assert np.all(np.abs(got - want) <= RTOL_REDUCE * np.abs(want) + 1e-30), np.max(np.abs(got - want) / np.abs(want))
+
+
+@pytest.mark.parametrize("shape,dims", [((1000,), ()), ((1000,), (0,)), ((19, 300), (1,)), ((19, 300), (0,)),
+                                        ((4, 5, 6), (1,)), ((4, 5, 6), (0, 2)), ((3, 4, 5, 6), (1, 3)),
+                                        ((3, 4, 5, 6), (0, 1, 2, 3)), ((3, 4, 5, 6), (-1,)), ((2, 3, 4, 5), (0, 3))])
+@pytest.mark.parametrize("mean", [False, True])
+def test_ttc_reduce_any_dims(ttc, shape, dims, mean):
+    rng = np.random.default_rng(5)
+    x = rng.uniform(-1, 1, shape).astype(np.float32)
+    X = dev(ttc, x)
+    want = oracle.reduce(x, dims, mean=mean, f64=True)
+    O = ttc.DeviceArray.empty(want.shape)
+    ttc.reduce(X.ptr, shape, dims, mean, O.ptr)
+    got = O.numpy()
+    assert np.allclose(got, want, rtol=RTOL_REDUCE, atol=1e-6)
+
+
+def test_segments_and_column_broadcast(ttc):
+    """8 segments (split chunks as views) of sigmoid(C) * relu(C + C), reduced
+    along dim 1 of the transposed view: r_i[j] = sum_c f(A[2048 i + c, j])."""
+    rng = np.random.default_rng(6)
+    R, C, nseg = 64, 96, 8
+    a = rng.uniform(-1, 1, (nseg * R, C)).astype(np.float32)
+    A = dev(ttc, a)
+    O = ttc.DeviceArray.empty((nseg, C))
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(ttc.OP_ADD, ttc.SRC_ACC), ttc.instr(ttc.OP_RELU),
+            ttc.instr(ttc.OP_SAVE, idx=0), ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(ttc.OP_SIGMOID),
+            ttc.instr(ttc.OP_MUL, ttc.SRC_SLOT, 0)]
+    ttc.eltwise_chain(ttc.chain_desc(R, C, [ttc.in_view(A.ptr, C, 1, R * C)], [], prog, reduce=ttc.REDUCE_COLS,
+                                     reduce_out=O.ptr, nseg=nseg, reduce_seg_stride=C))
+    y = oracle.multiply(oracle.sigmoid(a), oracle.relu(oracle.add(a, a)))
+    want = y.reshape(nseg, R, C).astype(np.float64).sum(axis=1)
+    assert np.allclose(O.numpy(), want, rtol=RTOL_REDUCE, atol=1e-6)
+    # column broadcast [R, 1] operand
+    col = rng.uniform(-1, 1, (R, 1)).astype(np.float32)
+    Cv = dev(ttc, col)
+    Y = ttc.DeviceArray.empty((R, C))
+    prog = [ttc.instr(ttc.OP_LOAD, idx=0), ttc.instr(ttc.OP_MUL, ttc.SRC_INPUT, 1), ttc.instr(ttc.OP_STORE, idx=0)]
+    ttc.eltwise_chain(ttc.chain_desc(R, C, [ttc.in_view(A.ptr, C), ttc.in_view(Cv.ptr, 1, 0)],
+                                     [ttc.out_view(Y.ptr, C)], prog))
+    assert np.array_equal(Y.numpy(), (a[:R] * col).astype(np.float32))
+
+
+@pytest.mark.parametrize("shape", [(1, 1), (23, 41), (64, 64), (1000, 1000), (129, 4097), (3, 16, 20)])
+def test_transpose_bit_exact(ttc, shape):
+    rng = np.random.default_rng(7)
+    x = rng.uniform(-1, 1, shape).astype(np.float32)
+    X = dev(ttc, x)
+    out_shape = list(shape)
+    out_shape[-1], out_shape[-2] = out_shape[-2], out_shape[-1]
+    Y = ttc.DeviceArray.empty(out_shape)
+    batch = int(np.prod(shape[:-2])) if len(shape) > 2 else 1
+    ttc.transpose(X.ptr, Y.ptr, batch, shape[-2], shape[-1])
+    assert np.array_equal(Y.numpy(), oracle.transpose(x))
+
+
+@pytest.mark.parametrize("shape,split,dim", [((10,), 3, 0), ((12, 17), 5, 0), ((12, 17), 5, 1), ((64, 256), 32, 1)])
+def test_split_chunks_as_strided_copies(ttc, shape, split, dim):
+    rng = np.random.default_rng(8)
+    x = rng.uniform(-1, 1, shape).astype(np.float32)
+    X = dev(ttc, x)
+    x2 = x.reshape(1, -1) if x.ndim == 1 else x
+    d = 1 if x.ndim == 1 else dim
+    for i, want in enumerate(oracle.split(x, split, dim)):
+        w2 = want.reshape(1, -1) if want.ndim == 1 else want
+        Y = ttc.DeviceArray.empty(w2.shape)
+        off = i * split * (1 if d == 1 else x2.shape[1])
+        ttc.copy2d(X.at(off), x2.shape[1], Y.ptr, w2.shape[1], w2.shape[0], w2.shape[1])
+        assert np.array_equal(Y.numpy(), w2)
+
+
+def _gemm_case(ttc, m, k, n, ta, tb, path, rng, act=None, bias=False):
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    a_st = np.ascontiguousarray(a.T) if ta else a
+    b_st = np.ascontiguousarray(b.T) if tb else b
+    A, B = dev(ttc, a_st), dev(ttc, b_st)
+    Cd = ttc.DeviceArray.empty((m, n))
+    epi = None
+    bias_v = rng.uniform(-0.1, 0.1, (1, n)).astype(np.float32)
+    if act or bias:
+        Bv = dev(ttc, bias_v)
+        prog, ins = [], []
+        if bias:
+            ins.append(ttc.in_view(Bv.ptr, 0))
+            prog.append(ttc.instr(ttc.OP_ADD, ttc.SRC_INPUT, 0))
+        if act == "relu":
+            prog.append(ttc.instr(ttc.OP_RELU))
+        if act == "sigmoid":
+            prog.append(ttc.instr(ttc.OP_SIGMOID))
+        prog.append(ttc.instr(ttc.OP_STORE, idx=0))
+        epi = ttc.chain_desc(m, n, ins, [ttc.out_view(Cd.ptr, n)], prog)
+    g = ttc.gemm(m, n, k, A.ptr, a_st.shape[1], B.ptr, b_st.shape[1], Cd.ptr, n, ta, tb, path, epi)
+    want = oracle.matmul(a_st, b_st, ta, tb)
+    if bias:
+        want = oracle.add(want, bias_v)
+    if act == "relu":
+        want = oracle.relu(want)
+    if act == "sigmoid":
+        want = oracle.sigmoid(want)
+    return Cd.numpy(), want, g
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1, 1), (2, 2, 2), (45, 67, 29), (128, 128, 128), (256, 512, 1024),
+                                   (257, 33, 130)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_gemm_ffma(ttc, m, k, n, ta, tb):
+    rng = np.random.default_rng(9)
+    got, want, _ = _gemm_case(ttc, m, k, n, ta, tb, ttc.GEMM_FFMA, rng)
+    assert normwise(got, want) <= RTOL_FFMA
+
+
+def test_gemm_known_answer(ttc):
+    # tests/cpp/integration/test_end_to_end.cpp:58-89: 2s . 3s = 12
+    A = dev(ttc, np.full((2, 2), 2, np.float32))
+    B = dev(ttc, np.full((2, 2), 3, np.float32))
+    C = ttc.DeviceArray.empty((2, 2))
+    ttc.gemm(2, 2, 2, A.ptr, 2, B.ptr, 2, C.ptr, 2, path=ttc.GEMM_FFMA)
+    assert np.all(C.numpy() == 12.0)
+
+
+@pytest.mark.parametrize("m,k,n", [(128, 32, 256), (256, 512, 1024), (256, 1024, 512), (384, 100, 300),
+                                   (1000, 260, 772), (128, 4096, 256)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_gemm_tf32(ttc, m, k, n, ta, tb):
+    rng = np.random.default_rng(10)
+    got, want, g = _gemm_case(ttc, m, k, n, ta, tb, ttc.GEMM_TF32, rng)
+    assert ttc.gemm_select_path(g) == ttc.GEMM_TF32
+    err = normwise(got, want)
+    assert err <= RTOL_TF32, err
+
+
+@pytest.mark.parametrize("path", ["ffma", "tf32"])
+@pytest.mark.parametrize("act", ["relu", "sigmoid", None])
+def test_gemm_epilogue_fused_mlp(ttc, path, act, golden):
+    """math::fused_mlp (fused_ops.cpp:39-61): bias then activation in the epilogue."""
+    rng = np.random.default_rng(12)
+    p = ttc.GEMM_FFMA if path == "ffma" else ttc.GEMM_TF32
+    got, want, _ = _gemm_case(ttc, 256, 512, 1024, 0, 0, p, rng, act=act, bias=True)
+    assert normwise(got, want) <= (RTOL_FFMA if path == "ffma" else RTOL_TF32)
+
+
+def test_gemm_golden_fused_mlp(ttc, golden):
+    x, w, b = golden["mm_a"], golden["mlp_w"], golden["mlp_b"]
+    X, Wd, Bd = dev(ttc, x), dev(ttc, w), dev(ttc, b)
+    Y = ttc.DeviceArray.empty((x.shape[0], w.shape[1]))
+    epi = ttc.chain_desc(x.shape[0], w.shape[1], [ttc.in_view(Bd.ptr, 0)], [ttc.out_view(Y.ptr, w.shape[1])],
+                         [ttc.instr(ttc.OP_ADD, ttc.SRC_INPUT, 0), ttc.instr(ttc.OP_RELU),
+                          ttc.instr(ttc.OP_STORE, idx=0)])
+    ttc.gemm(x.shape[0], w.shape[1], x.shape[1], X.ptr, x.shape[1], Wd.ptr, w.shape[1], path=ttc.GEMM_FFMA,
+             epilogue=epi)
+    assert normwise(Y.numpy(), golden["mlp_relu_y"]) <= RTOL_FFMA
+
+
+def test_invalid_descriptors_are_errors(ttc):
+    X = ttc.DeviceArray.empty((4, 4))
+    bad = ttc.chain_desc(4, 4, [ttc.in_view(X.ptr, 4)], [], [ttc.instr(ttc.OP_RELU)])
+    with pytest.raises(ttc.TTCError) as e:
+        ttc.eltwise_chain(bad)
+    assert e.value.code == ttc.ERR_INVALID
+    bad = ttc.chain_desc(4, 4, [ttc.in_view(X.ptr, 4, 2)], [], [ttc.instr(ttc.OP_LOAD)])
+    with pytest.raises(ttc.TTCError):
+        ttc.eltwise_chain(bad)
+    with pytest.raises(ttc.TTCError):
+        ttc.gemm(4, 4, 4, X.ptr, 2, X.ptr, 4, X.ptr, 4)

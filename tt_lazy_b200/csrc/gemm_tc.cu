@@ -1,0 +1,425 @@
+// gemm_tc.cu -- TF32 tensor-core GEMM for sm_100a: tcgen05.mma (kind::tf32)
+// with accumulators in tensor memory, operands staged by TMA, and the
+// element-wise epilogue program applied on the way out of TMEM.
+//
+// Replaces math::matmul (src/backend/cpu/matmul.cpp:36-85) and
+// math::fused_mlp (src/backend/cpu/fused_ops.cpp:8-64) on the fast path:
+// norm-wise relative error ~1e-3 (TF32 keeps 10 mantissa bits of each
+// operand; accumulation is fp32).
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0     TMA producer: per k-block, one TMA box (K-major operand) or
+//              one box per 32 columns (MN-major operand) into a 4-stage ring
+//              of shared-memory buffers (128-byte swizzle).
+//   warp 1     allocates 512 TMEM columns (two 128x256 fp32 accumulators),
+//              then one lane issues 4 tcgen05.mma (K = 8 each) per k-block and
+//              commits each stage back to the producer and each finished tile
+//              to the epilogue.
+//   warps 2-5  epilogue: tcgen05.ld 32 columns at a time (each warp reads
+//              its own 32 TMEM lanes = 32 output rows), run the epilogue
+//              program (bias / relu / sigmoid / store), release the
+//              accumulator so the MMA warp can start the tile after next.
+// The tile order is grouped by 16 row-blocks so the A and B panels a wave of
+// CTAs touches stay in the 126 MB L2.
+//
+// No TMA multicast and no clusters: the kernel is also used by every rank of
+// a multi-GPU run. Every mbarrier wait is bounded (about 2 s); an expired
+// wait records an error in a host-mapped status word, lets the other roles
+// time out too, waits for its own TMA loads, frees TMEM and returns.
+#include <cuda.h>
+
+#include <cstring>
+
+#include "ttc_internal.cuh"
+
+namespace ttc {
+
+int device_status_ptr(int** dptr);
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 4;  // 16 KB
+constexpr int B_BYTES = BN * BK * 4;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int kThreads = 192;
+constexpr int GROUP_M = 16;
+constexpr long long kWaitLimit = 4000000000ll;  // clock cycles (~2 s)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+
+struct TcParams {
+    CUtensorMap tma_a;
+    CUtensorMap tma_b;
+    int M, N, K;
+    int m_blocks, n_blocks, k_blocks;
+    int a_mn_major, b_mn_major;
+    unsigned idesc;
+    int* status;
+    DProgram epi;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with the given parity; false when it expired.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity))
+        if (clock64() - t0 > kWaitLimit) return false;
+    return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+            dst),
+        "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
+        : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: register j of lane l = TMEM
+// (lane base + l, column + j).
+__device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout: start
+// address, leading / stride byte offsets in 16-byte units, version 1,
+// layout type 2 = SWIZZLE_128B).
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)2 << 61;
+    return d;
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int m_blocks, int n_blocks, int& mb, int& nb) {
+    const int per_group = GROUP_M * n_blocks;
+    const int group = tile / per_group;
+    const int first_m = group * GROUP_M;
+    const int gm = min(GROUP_M, m_blocks - first_m);
+    const int local = tile - group * per_group;
+    mb = first_m + local % gm;
+    nb = local / gm;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+    auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
+    auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(full_bar(s), 1);
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 4);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int num_tiles = p.m_blocks * p.n_blocks;
+    bool failed = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&p.tma_a) : "memory");
+            asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)&p.tma_b) : "memory");
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && !failed; tile += gridDim.x) {
+                int mb, nb;
+                tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1)) {
+                        failed = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
+                    const uint32_t a_dst = sbase + stage * STAGE_BYTES, b_dst = a_dst + A_BYTES;
+                    if (!p.a_mn_major) {
+                        tma_load_2d(a_dst, &p.tma_a, full_bar(stage), kb * BK, mb * BM);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BM / 32; ++j)
+                            tma_load_2d(a_dst + j * (BK * 128), &p.tma_a, full_bar(stage), mb * BM + 32 * j, kb * BK);
+                    }
+                    if (!p.b_mn_major) {
+                        tma_load_2d(b_dst, &p.tma_b, full_bar(stage), kb * BK, nb * BN);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 32; ++j)
+                            tma_load_2d(b_dst + j * (BK * 128), &p.tma_b, full_bar(stage), nb * BN + 32 * j, kb * BK);
+                    }
+                    ++issued;
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Never leave with loads in flight: wait (bounded) for the most
+            // recent load of every stage to land.
+            const long long last = issued < STAGES ? issued : STAGES;
+            for (long long i = 0; i < last; ++i) {
+                const long long n = issued - 1 - i;
+                const int s = (int)(n % STAGES);
+                const uint32_t ph = (uint32_t)((n / STAGES) & 1);
+                if (!mbar_wait(full_bar(s), ph)) failed = true;
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16;
+            const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16;
+            const uint32_t a_kstep = p.a_mn_major ? 8 * 128 : 32;
+            const uint32_t b_kstep = p.b_mn_major ? 8 * 128 : 32;
+            int stage = 0;
+            uint32_t phase = 0;
+            int t = 0;
+            for (int tile = blockIdx.x; tile < num_tiles && !failed; tile += gridDim.x, ++t) {
+                const int b = t & 1;
+                const uint32_t acc_phase = (t >> 1) & 1;
+                if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase)) {
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_s = sbase + stage * STAGE_BYTES, b_s = a_s + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 8; ++k) {
+                        const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, 1024);
+                        const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, 1024);
+                        tc_mma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    tc_commit(empty_bar(stage));
+                    if (++stage == STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (failed) break;
+                tc_commit(tfull_bar(b));
+            }
+        }
+    } else {
+        const int q = warp & 3;  // this warp's quarter of the 128 TMEM lanes
+        int t = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+            int mb, nb;
+            tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+            const int b = t & 1;
+            const uint32_t acc_phase = (t >> 1) & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase));
+            if (!ok) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            const long long row = (long long)mb * BM + q * 32 + lane;
+            for (int c = 0; c < BN / 32; ++c) {
+                uint32_t r[32];
+                tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), r);
+                tc_wait_ld();
+                const long long col0 = (long long)nb * BN + c * 32;
+                if (col0 >= p.N) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float v[4][4];
+                    long long rr[4], cc[4];
+                    bool vv[4];
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        rr[g] = row;
+                        cc[g] = col0 + h * 16 + g * 4;
+                        vv[g] = row < p.M && cc[g] < p.N;
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) v[g][w] = __uint_as_float(r[h * 16 + g * 4 + w]);
+                    }
+                    run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tempty_bar(b));
+        }
+    }
+
+    if (failed) *(volatile int*)p.status = 1;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                     : "memory");
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// 2-D fp32 tensor map over a row-major matrix with `outer` rows of `inner`
+// elements (row pitch ld elements), box {32, box_outer}, 128-byte swizzle,
+// out-of-bounds reads filled with zeros.
+int make_map(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld, int box_outer) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(TTC_ERR_CUDA, "tt_cuda: cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+    cuuint32_t box[2] = {32, (cuuint32_t)box_outer};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)ptr, dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TTC_ERR_CUDA, "tt_cuda: cuTensorMapEncodeTiled failed (%d) for %lld x %lld, ld %lld", (int)r,
+                         outer, inner, ld);
+    return TTC_OK;
+}
+
+}  // namespace
+
+bool tf32_supported(const ttc_gemm_desc& d, const DProgram& epi, bool epi_vec) {
+    (void)epi;
+    if (d.M < 1 || d.N < 1 || d.K < 1) return false;
+    if (!epi_vec) return false;
+    if (d.lda % 4 || d.ldb % 4) return false;
+    if (((uintptr_t)d.a & 15) || ((uintptr_t)d.b & 15)) return false;
+    if ((long long)d.M * d.N < 128 * 64) return false;  // too small to fill a tensor-core tile
+    return true;
+}
+
+int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr_set = true;
+    }
+    TcParams p;
+    std::memset(&p, 0, sizeof p);
+    p.a_mn_major = d.trans_a ? 1 : 0;
+    p.b_mn_major = d.trans_b ? 0 : 1;
+    // A: logical [M, K]; K-major when stored [M, K] (trans_a = 0).
+    if (!p.a_mn_major) {
+        if (int rc = make_map(&p.tma_a, d.a, d.K, d.M, d.lda, BM)) return rc;
+    } else {
+        if (int rc = make_map(&p.tma_a, d.a, d.M, d.K, d.lda, BK)) return rc;
+    }
+    // B: logical [K, N]; MN-major when stored [K, N] (trans_b = 0).
+    if (p.b_mn_major) {
+        if (int rc = make_map(&p.tma_b, d.b, d.N, d.K, d.ldb, BK)) return rc;
+    } else {
+        if (int rc = make_map(&p.tma_b, d.b, d.K, d.N, d.ldb, BN)) return rc;
+    }
+    p.M = d.M;
+    p.N = d.N;
+    p.K = d.K;
+    p.m_blocks = (d.M + BM - 1) / BM;
+    p.n_blocks = (d.N + BN - 1) / BN;
+    p.k_blocks = (d.K + BK - 1) / BK;
+    p.idesc = (1u << 4)                       // D format: f32
+              | (2u << 7) | (2u << 10)        // A, B format: tf32
+              | ((unsigned)p.a_mn_major << 15) | ((unsigned)p.b_mn_major << 16) |
+              ((unsigned)(BN >> 3) << 17)     // N
+              | ((unsigned)(BM >> 4) << 24);  // M
+    if (int rc = device_status_ptr(&p.status)) return rc;
+    p.epi = epi;
+    const long long tiles = (long long)p.m_blocks * p.n_blocks;
+    if (tiles > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many GEMM tiles");
+    const int grid = (int)(tiles < rt().sm_count ? tiles : rt().sm_count);
+    tf32_gemm_kernel<<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
+    count_launch();
+    return check_cuda(cudaGetLastError(), "TF32 GEMM launch");
+}
+
+}  // namespace ttc

@@ -1,0 +1,358 @@
+// runtime.cu -- tt_cuda_lib runtime: error state, device/stream selection,
+// stream-ordered device memory (the replacement of the reference's host
+// MemoryPool, src/core/MemoryManager.cpp:46-133), copies, the internal
+// workspace, and decoding of element-wise programs.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <unordered_map>
+
+#include "ttc_internal.cuh"
+
+namespace ttc {
+
+namespace {
+thread_local std::string g_last_error;
+Runtime g_rt;
+std::unordered_map<void*, size_t> g_sizes;  // live ttc_malloc blocks (stats)
+}  // namespace
+
+Runtime& rt() { return g_rt; }
+
+int set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+void clear_error() { g_last_error.clear(); }
+
+int check_cuda(cudaError_t e, const char* what) {
+    if (e == cudaSuccess) return TTC_OK;
+    const int code = (e == cudaErrorMemoryAllocation) ? TTC_ERR_OUT_OF_MEMORY : TTC_ERR_CUDA;
+    return set_error(code, "tt_cuda: %s failed: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+int workspace(size_t bytes, void** out) {
+    Runtime& r = rt();
+    if (bytes > r.workspace_bytes) {
+        if (r.workspace) {
+            // The old buffer may still be read by queued kernels: free in stream order.
+            TTC_CUDA(cudaFreeAsync(r.workspace, r.stream));
+            r.workspace = nullptr;
+            r.workspace_bytes = 0;
+        }
+        size_t want = bytes < (1u << 20) ? (1u << 20) : bytes;
+        TTC_CUDA(cudaMallocAsync(&r.workspace, want, r.stream));
+        r.workspace_bytes = want;
+    }
+    *out = r.workspace;
+    return TTC_OK;
+}
+
+// A host-mapped status word that kernels with bounded waits set when a wait
+// expires. The host reads it after every synchronisation.
+namespace {
+int* g_status_host = nullptr;
+int* g_status_dev = nullptr;
+}  // namespace
+
+int device_status_ptr(int** dptr) {
+    if (!g_status_host) {
+        TTC_CUDA(cudaHostAlloc((void**)&g_status_host, sizeof(int), cudaHostAllocMapped));
+        *g_status_host = 0;
+        TTC_CUDA(cudaHostGetDevicePointer((void**)&g_status_dev, g_status_host, 0));
+    }
+    *dptr = g_status_dev;
+    return TTC_OK;
+}
+
+// After a synchronisation: turn a recorded device-side wait expiry into an error.
+int check_device_status() {
+    if (g_status_host && *(volatile int*)g_status_host) {
+        *(volatile int*)g_status_host = 0;
+        return set_error(TTC_ERR_TIMEOUT,
+                         "tt_cuda: a kernel's bounded wait expired (pipeline stalled); its output is invalid");
+    }
+    return TTC_OK;
+}
+
+FastDiv make_fastdiv(unsigned d) {
+    FastDiv f{d, 0, 0};
+    unsigned s = 0;
+    while ((1ull << s) < d) ++s;
+    f.s = s;
+    f.m = (unsigned)((((1ull << 32) * ((1ull << s) - d)) / d) + 1);
+    return f;
+}
+
+int decode_program(const ttc_chain_desc& d, bool acc_preloaded, DProgram* out) {
+    std::memset(out, 0, sizeof *out);
+    if (d.n_instr < 0 || d.n_instr > TTC_CHAIN_MAX_INSTR)
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: program length %d outside [0, %d]", d.n_instr,
+                         TTC_CHAIN_MAX_INSTR);
+    if (d.n_inputs < 0 || d.n_inputs > TTC_CHAIN_MAX_INPUTS || d.n_outputs < 0 ||
+        d.n_outputs > TTC_CHAIN_MAX_OUTPUTS)
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: %d inputs / %d outputs exceed %d / %d", d.n_inputs,
+                         d.n_outputs, TTC_CHAIN_MAX_INPUTS, TTC_CHAIN_MAX_OUTPUTS);
+    out->n_instr = d.n_instr;
+    out->n_in = d.n_inputs;
+    out->n_out = d.n_outputs;
+    for (int i = 0; i < d.n_inputs; ++i) {
+        const ttc_in_view& v = d.inputs[i];
+        if (!v.ptr) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: input %d is NULL", i);
+        if (v.col_stride != 0 && v.col_stride != 1)
+            return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: input %d col_stride %lld not 0 or 1", i,
+                             (long long)v.col_stride);
+        if (v.row_stride < 0 || v.seg_stride < 0)
+            return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: input %d has a negative stride", i);
+        out->in[i] = DInView{v.ptr, v.row_stride, v.col_stride, v.seg_stride};
+    }
+    for (int i = 0; i < d.n_outputs; ++i) {
+        const ttc_out_view& v = d.outputs[i];
+        if (!v.ptr) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: output %d is NULL", i);
+        if (v.row_stride < 0 || v.seg_stride < 0)
+            return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: output %d has a negative stride", i);
+        out->out[i] = DOutView{v.ptr, v.row_stride, v.seg_stride};
+    }
+    bool acc_defined = acc_preloaded;
+    bool slot_defined[TTC_CHAIN_SLOTS] = {false, false, false, false};
+    for (int pc = 0; pc < d.n_instr; ++pc) {
+        const ttc_instr& in = d.program[pc];
+        uint8_t op = 0, arg = 0;
+        auto need_acc = [&]() -> int {
+            if (!acc_defined)
+                return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d reads acc before any LOAD", pc);
+            return TTC_OK;
+        };
+        switch (in.op) {
+            case TTC_OP_LOAD:
+                if (in.idx >= d.n_inputs)
+                    return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d loads input %d of %d", pc, in.idx,
+                                     d.n_inputs);
+                op = D_LOAD;
+                arg = in.idx;
+                acc_defined = true;
+                break;
+            case TTC_OP_RELU:
+            case TTC_OP_SIGMOID:
+                if (int rc = need_acc()) return rc;
+                op = in.op == TTC_OP_RELU ? D_RELU : D_SIGMOID;
+                break;
+            case TTC_OP_ADD:
+            case TTC_OP_MUL: {
+                if (int rc = need_acc()) return rc;
+                const bool add = in.op == TTC_OP_ADD;
+                if (in.src == TTC_SRC_ACC) {
+                    op = add ? D_ADD_ACC : D_MUL_ACC;
+                } else if (in.src == TTC_SRC_INPUT) {
+                    if (in.idx >= d.n_inputs)
+                        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d reads input %d of %d", pc,
+                                         in.idx, d.n_inputs);
+                    op = add ? D_ADD_IN : D_MUL_IN;
+                    arg = in.idx;
+                } else if (in.src == TTC_SRC_SLOT) {
+                    if (in.idx >= TTC_CHAIN_SLOTS || !slot_defined[in.idx])
+                        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d reads unset slot %d", pc,
+                                         in.idx);
+                    op = (uint8_t)((add ? D_ADD_S0 : D_MUL_S0) + in.idx);
+                } else {
+                    return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d has source kind %d", pc, in.src);
+                }
+                break;
+            }
+            case TTC_OP_SAVE:
+                if (int rc = need_acc()) return rc;
+                if (in.idx >= TTC_CHAIN_SLOTS)
+                    return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d saves to slot %d", pc, in.idx);
+                op = (uint8_t)(D_SAVE0 + in.idx);
+                slot_defined[in.idx] = true;
+                break;
+            case TTC_OP_STORE:
+                if (int rc = need_acc()) return rc;
+                if (in.idx >= d.n_outputs)
+                    return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d stores to output %d of %d", pc,
+                                     in.idx, d.n_outputs);
+                op = D_STORE;
+                arg = in.idx;
+                break;
+            default:
+                return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d has unknown opcode %d", pc, in.op);
+        }
+        out->op[pc] = op;
+        out->arg[pc] = arg;
+    }
+    if (!acc_defined && d.reduce != TTC_REDUCE_NONE)
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: reduction of a program that never loads");
+    return TTC_OK;
+}
+
+}  // namespace ttc
+
+using namespace ttc;
+
+extern "C" {
+
+const char* ttc_last_error(void) { return g_last_error.c_str(); }
+
+int ttc_version(void) { return (0 << 16) | 1; }
+
+int ttc_device_count(int* count) {
+    if (!count) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: count is NULL");
+    cudaError_t e = cudaGetDeviceCount(count);
+    if (e != cudaSuccess) {
+        *count = 0;
+        cudaGetLastError();
+        return check_cuda(e, "cudaGetDeviceCount");
+    }
+    return TTC_OK;
+}
+
+int ttc_init(int device) {
+    Runtime& r = rt();
+    if (r.initialized) {
+        if (r.device == device) return TTC_OK;
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: already initialised on device %d (asked %d)",
+                         r.device, device);
+    }
+    int n = 0;
+    TTC_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n)
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: device %d outside [0, %d)", device, n);
+    TTC_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    TTC_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: device %d is sm_%d%d; this build targets sm_100a (B200)",
+                         device, prop.major, prop.minor);
+    r.sm_count = prop.multiProcessorCount;
+    TTC_CUDA(cudaStreamCreateWithFlags(&r.own_stream, cudaStreamNonBlocking));
+    r.stream = r.own_stream;
+    // Keep freed pool memory cached in the process: the tape frees and
+    // re-allocates the same sizes every evaluation.
+    cudaMemPool_t pool;
+    TTC_CUDA(cudaDeviceGetDefaultMemPool(&pool, device));
+    uint64_t threshold = UINT64_MAX;
+    TTC_CUDA(cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &threshold));
+    r.device = device;
+    r.initialized = true;
+    return TTC_OK;
+}
+
+int ttc_shutdown(void) {
+    Runtime& r = rt();
+    if (!r.initialized) return TTC_OK;
+    cudaStreamSynchronize(r.stream);
+    if (r.workspace) cudaFree(r.workspace);
+    r.workspace = nullptr;
+    r.workspace_bytes = 0;
+    if (r.own_stream) cudaStreamDestroy(r.own_stream);
+    r.own_stream = r.stream = nullptr;
+    r.initialized = false;
+    r.device = -1;
+    return TTC_OK;
+}
+
+void* ttc_get_stream(void) { return (void*)rt().stream; }
+
+int ttc_set_stream(void* s) {
+    TTC_REQUIRE_INIT();
+    rt().stream = s ? (cudaStream_t)s : rt().own_stream;
+    return TTC_OK;
+}
+
+int ttc_synchronize(void) {
+    TTC_REQUIRE_INIT();
+    TTC_CUDA(cudaStreamSynchronize(rt().stream));
+    return check_device_status();
+}
+
+int ttc_malloc(size_t bytes, void** dptr) {
+    TTC_REQUIRE_INIT();
+    if (!dptr) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: dptr is NULL");
+    *dptr = nullptr;
+    if (bytes == 0) return TTC_OK;
+    // Round to 256 B so every buffer is TMA- and float4-aligned.
+    size_t sz = (bytes + 255) & ~(size_t)255;
+    cudaError_t e = cudaMallocAsync(dptr, sz, rt().stream);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(e == cudaErrorMemoryAllocation ? TTC_ERR_OUT_OF_MEMORY : TTC_ERR_CUDA,
+                         "tt_cuda: cannot allocate %zu bytes of device memory: %s", bytes, cudaGetErrorString(e));
+    }
+    Runtime& r = rt();
+    g_sizes[*dptr] = sz;
+    r.bytes_in_use += sz;
+    if (r.bytes_in_use > r.peak_bytes) r.peak_bytes = r.bytes_in_use;
+    return TTC_OK;
+}
+
+int ttc_free(void* dptr) {
+    TTC_REQUIRE_INIT();
+    if (!dptr) return TTC_OK;
+    auto it = g_sizes.find(dptr);
+    if (it == g_sizes.end())
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: ttc_free of %p, which ttc_malloc did not return", dptr);
+    TTC_CUDA(cudaFreeAsync(dptr, rt().stream));
+    rt().bytes_in_use -= it->second;
+    g_sizes.erase(it);
+    return TTC_OK;
+}
+
+int ttc_memcpy_h2d(void* dst, const void* src, size_t bytes) {
+    TTC_REQUIRE_INIT();
+    if (bytes == 0) return TTC_OK;
+    TTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, rt().stream));
+    return TTC_OK;
+}
+
+int ttc_memcpy_d2h(void* dst, const void* src, size_t bytes) {
+    TTC_REQUIRE_INIT();
+    if (bytes == 0) return TTC_OK;
+    TTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, rt().stream));
+    TTC_CUDA(cudaStreamSynchronize(rt().stream));
+    return check_device_status();
+}
+
+int ttc_memcpy_d2d(void* dst, const void* src, size_t bytes) {
+    TTC_REQUIRE_INIT();
+    if (bytes == 0) return TTC_OK;
+    TTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, rt().stream));
+    return TTC_OK;
+}
+
+int ttc_memset_zero(void* dst, size_t bytes) {
+    TTC_REQUIRE_INIT();
+    if (bytes == 0) return TTC_OK;
+    TTC_CUDA(cudaMemsetAsync(dst, 0, bytes, rt().stream));
+    return TTC_OK;
+}
+
+int ttc_host_alloc(size_t bytes, void** hptr) {
+    TTC_REQUIRE_INIT();
+    if (!hptr) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: hptr is NULL");
+    TTC_CUDA(cudaHostAlloc(hptr, bytes, cudaHostAllocDefault));
+    return TTC_OK;
+}
+
+int ttc_host_free(void* hptr) {
+    TTC_REQUIRE_INIT();
+    if (hptr) TTC_CUDA(cudaFreeHost(hptr));
+    return TTC_OK;
+}
+
+int ttc_get_memory_stats(ttc_memory_stats* out) {
+    if (!out) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: out is NULL");
+    Runtime& r = rt();
+    out->bytes_in_use = r.bytes_in_use;
+    out->peak_bytes = r.peak_bytes;
+    out->workspace_bytes = r.workspace_bytes;
+    out->kernels_launched = r.kernels;
+    return TTC_OK;
+}
+
+}  // extern "C"

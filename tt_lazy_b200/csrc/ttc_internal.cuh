@@ -1,0 +1,240 @@
+// ttc_internal.cuh -- shared internals of tt_cuda_lib: error plumbing, the
+// runtime state, and the element-wise program interpreter that the chain
+// kernel and every GEMM epilogue run.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/tt_cuda.h"
+
+// ------------------------------------------------------------------ errors
+namespace ttc {
+
+int set_error(int code, const char* fmt, ...);
+int check_cuda(cudaError_t e, const char* what);
+void clear_error();
+
+struct Runtime {
+    bool initialized = false;
+    int device = -1;
+    int sm_count = 0;
+    cudaStream_t own_stream = nullptr;
+    cudaStream_t stream = nullptr;
+    void* workspace = nullptr;  // grow-only internal scratch (reduction partials)
+    size_t workspace_bytes = 0;
+    size_t bytes_in_use = 0, peak_bytes = 0;
+    unsigned long long kernels = 0;
+};
+Runtime& rt();
+// Scratch of at least `bytes`, valid until the next call that asks for more.
+int workspace(size_t bytes, void** out);
+inline void count_launch(unsigned n = 1) { rt().kernels += n; }
+
+}  // namespace ttc
+
+#define TTC_REQUIRE_INIT()                                                                  \
+    do {                                                                                    \
+        if (!ttc::rt().initialized)                                                        \
+            return ttc::set_error(TTC_ERR_NOT_INITIALIZED, "tt_cuda: ttc_init() not called"); \
+    } while (0)
+
+#define TTC_CUDA(call)                                                  \
+    do {                                                                \
+        cudaError_t _e = (call);                                        \
+        if (_e != cudaSuccess) return ttc::check_cuda(_e, #call);        \
+    } while (0)
+
+// ------------------------------------------------ device program (decoded)
+// The C-ABI program (ttc_instr: op, src, idx) is decoded on the host into a
+// flat opcode per step so that each step is one warp-uniform switch case
+// working on compile-time registers (no runtime-indexed register arrays,
+// which would spill to local memory).
+namespace ttc {
+
+enum DOp : uint8_t {
+    D_LOAD = 0,
+    D_RELU,
+    D_SIGMOID,
+    D_ADD_ACC,
+    D_ADD_IN,
+    D_ADD_S0,
+    D_ADD_S1,
+    D_ADD_S2,
+    D_ADD_S3,
+    D_MUL_ACC,
+    D_MUL_IN,
+    D_MUL_S0,
+    D_MUL_S1,
+    D_MUL_S2,
+    D_MUL_S3,
+    D_SAVE0,
+    D_SAVE1,
+    D_SAVE2,
+    D_SAVE3,
+    D_STORE,
+    D_NUM_OPS
+};
+
+struct DInView {
+    const float* ptr;
+    long long sr, sc, sseg;
+};
+struct DOutView {
+    float* ptr;
+    long long sr, sseg;
+};
+
+struct DProgram {
+    int n_instr;
+    int n_in, n_out;
+    uint8_t op[TTC_CHAIN_MAX_INSTR];
+    uint8_t arg[TTC_CHAIN_MAX_INSTR];
+    DInView in[TTC_CHAIN_MAX_INPUTS];
+    DOutView out[TTC_CHAIN_MAX_OUTPUTS];
+};
+
+// Validates and decodes `d` (the shape part is checked by the caller).
+// `acc_preloaded`: the GEMM epilogue case -- acc holds the product at entry.
+int decode_program(const ttc_chain_desc& d, bool acc_preloaded, DProgram* out);
+
+// 32-bit unsigned division by an invariant divisor (Granlund & Montgomery,
+// "Division by invariant integers using multiplication", PLDI 1994, sec. 4):
+// q = (umulhi(n, m) + n) >> s, exact for n < 2^31.
+struct FastDiv {
+    unsigned d, m, s;
+};
+FastDiv make_fastdiv(unsigned d);
+
+#ifdef __CUDACC__
+__device__ __forceinline__ unsigned fdiv(unsigned n, const FastDiv& f) {
+    return (__umulhi(n, f.m) + n) >> f.s;
+}
+
+// --------------------------------------------------------------------------
+// Interpreter. A thread evaluates G groups of W consecutive columns (W = 4:
+// one 128-bit access per operand per group; W = 1: scalar path). Group g
+// sits at (seg, row[g], col[g]); invalid groups skip every memory access.
+// Every arithmetic step is a single IEEE op; the translation units that use
+// this are compiled with -fmad=false so no multiply-add pair is contracted.
+template <int W>
+__device__ __forceinline__ void load_group(const DInView& v, long long seg, long long row, long long col,
+                                           float (&dst)[W]) {
+    const float* p = v.ptr + seg * v.sseg + row * v.sr;
+    if constexpr (W == 4) {
+        if (v.sc == 0) {
+            const float s = __ldg(p);
+            dst[0] = dst[1] = dst[2] = dst[3] = s;
+        } else {
+            const float4 q = __ldg(reinterpret_cast<const float4*>(p + col));
+            dst[0] = q.x;
+            dst[1] = q.y;
+            dst[2] = q.z;
+            dst[3] = q.w;
+        }
+    } else {
+        dst[0] = __ldg(p + col * v.sc);
+    }
+}
+
+template <int W>
+__device__ __forceinline__ void store_group(const DOutView& v, long long seg, long long row, long long col,
+                                            const float (&src)[W]) {
+    float* p = v.ptr + seg * v.sseg + row * v.sr + col;
+    if constexpr (W == 4) {
+        *reinterpret_cast<float4*>(p) = make_float4(src[0], src[1], src[2], src[3]);
+    } else {
+        p[0] = src[0];
+    }
+}
+
+__device__ __forceinline__ float op_relu(float x) { return (0.0f < x) ? x : 0.0f; }
+__device__ __forceinline__ float op_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// Applies f(g, w) to every element. Arithmetic runs on all groups (invalid
+// groups compute on zeros and are never stored or summed).
+template <int G, int W, class F>
+__device__ __forceinline__ void each(F&& f) {
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int w = 0; w < W; ++w) f(g, w);
+}
+
+template <int G, int W>
+__device__ __forceinline__ void run_program(const DProgram& P, float (&acc)[G][W], long long seg,
+                                            const long long (&row)[G], const long long (&col)[G],
+                                            const bool (&valid)[G]) {
+    float s0[G][W], s1[G][W], s2[G][W], s3[G][W];
+    each<G, W>([&](int g, int w) { s0[g][w] = s1[g][w] = s2[g][w] = s3[g][w] = 0.0f; });
+
+    for (int pc = 0; pc < P.n_instr; ++pc) {
+        const int a = P.arg[pc];
+        switch (P.op[pc]) {
+            case D_LOAD:
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (valid[g]) load_group<W>(P.in[a], seg, row[g], col[g], acc[g]);
+                break;
+            case D_RELU: each<G, W>([&](int g, int w) { acc[g][w] = op_relu(acc[g][w]); }); break;
+            case D_SIGMOID: each<G, W>([&](int g, int w) { acc[g][w] = op_sigmoid(acc[g][w]); }); break;
+            case D_ADD_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + acc[g][w]; }); break;
+            case D_MUL_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * acc[g][w]; }); break;
+            case D_ADD_IN: {
+                float t[G][W];
+                each<G, W>([&](int g, int w) { t[g][w] = 0.0f; });
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (valid[g]) load_group<W>(P.in[a], seg, row[g], col[g], t[g]);
+                each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + t[g][w]; });
+                break;
+            }
+            case D_MUL_IN: {
+                float t[G][W];
+                each<G, W>([&](int g, int w) { t[g][w] = 0.0f; });
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (valid[g]) load_group<W>(P.in[a], seg, row[g], col[g], t[g]);
+                each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * t[g][w]; });
+                break;
+            }
+            case D_ADD_S0: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s0[g][w]; }); break;
+            case D_ADD_S1: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s1[g][w]; }); break;
+            case D_ADD_S2: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s2[g][w]; }); break;
+            case D_ADD_S3: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s3[g][w]; }); break;
+            case D_MUL_S0: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s0[g][w]; }); break;
+            case D_MUL_S1: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s1[g][w]; }); break;
+            case D_MUL_S2: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s2[g][w]; }); break;
+            case D_MUL_S3: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s3[g][w]; }); break;
+            case D_SAVE0: each<G, W>([&](int g, int w) { s0[g][w] = acc[g][w]; }); break;
+            case D_SAVE1: each<G, W>([&](int g, int w) { s1[g][w] = acc[g][w]; }); break;
+            case D_SAVE2: each<G, W>([&](int g, int w) { s2[g][w] = acc[g][w]; }); break;
+            case D_SAVE3: each<G, W>([&](int g, int w) { s3[g][w] = acc[g][w]; }); break;
+            case D_STORE:
+#pragma unroll
+                for (int g = 0; g < G; ++g)
+                    if (valid[g]) store_group<W>(P.out[a], seg, row[g], col[g], acc[g]);
+                break;
+            default:
+                break;
+        }
+    }
+}
+
+// Warp / block sums used by the reductions (fixed shuffle order: the result
+// does not depend on scheduling, so reductions are run-to-run deterministic).
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+#endif  // __CUDACC__
+
+}  // namespace ttc
