@@ -73,6 +73,7 @@ def lib():
         L.orc_last_error.restype = C.c_char_p
         L.orc_relu.argtypes = [_f32p, _f32p, C.c_size_t]
         L.orc_sigmoid.argtypes = [_f32p, _f32p, C.c_size_t]
+        L.orc_sigmoid_cr.argtypes = [_f32p, _f32p, C.c_size_t]
         for fn in (L.orc_add, L.orc_multiply):
             fn.argtypes = [_f32p, _u32p, C.c_int, _f32p, _u32p, C.c_int, _f32p]
         L.orc_matmul.argtypes = [_f32p, C.c_uint32, C.c_uint32, _f32p, C.c_uint32, C.c_uint32,
@@ -125,6 +126,14 @@ def sigmoid(x):
     x = _f32(x)
     out = np.empty_like(x)
     _chk(lib().orc_sigmoid(x.reshape(-1), out.reshape(-1), x.size), lib())
+    return out
+
+
+def sigmoid_cr(x):
+    """README sigmoid with a correctly rounded expf (see oracle.h)."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    _chk(lib().orc_sigmoid_cr(x.reshape(-1), out.reshape(-1), x.size), lib())
     return out
 
 

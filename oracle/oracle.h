@@ -34,6 +34,10 @@ int orc_relu(const float* x, float* out, size_t n);
 /* README.md:332 -- 1.0f / (1.0f + std::exp(-x)); std::exp(float) is expf. */
 int orc_sigmoid(const float* x, float* out, size_t n);
 
+/* README.md:332 with e^-x correctly rounded (float)exp((double)-x): the
+ * formula's value independent of the libm's expf rounding. */
+int orc_sigmoid_cr(const float* x, float* out, size_t n);
+
 /* src/backend/cpu/eltwise.cpp:29-83 -- same-shape add, or [N,M] + [1,M]. */
 int orc_add(const float* a, const uint32_t* ashape, int arank,
             const float* b, const uint32_t* bshape, int brank, float* out);

@@ -62,14 +62,24 @@ def test_relu_bit_exact(ttc, shape):
     assert np.array_equal(got.view(np.int32), oracle.relu(x).view(np.int32))
 
 
-def test_sigmoid_within_2ulp(ttc, golden):
-    got = run_unary(ttc, ttc.OP_SIGMOID, golden["sig_x"].reshape(1, -1))
-    assert ulp_dist(got.ravel(), golden["sig_y"]).max() <= 2
+def test_sigmoid_ulp(ttc, golden):
+    """README.md:332 formula 1/(1+exp(-x)). Against the formula with a
+    correctly rounded expf the kernel is within 1 ulp (bit-identical almost
+    everywhere). glibc's expf, which the README recipe compiles to on the
+    CPU, is itself 1 ulp off on ~0.07% of inputs; there the division can
+    amplify that to 3 ulp of sigmoid, so against it the bound is 2 ulp on all
+    but <0.1% of elements and 3 ulp everywhere."""
     rng = np.random.default_rng(1)
-    x = rng.uniform(-30, 30, (2048, 2048)).astype(np.float32)
-    got = run_unary(ttc, ttc.OP_SIGMOID, x)
-    d = ulp_dist(got, oracle.sigmoid(x))
-    assert d.max() <= 2, d.max()
+    for x in (golden["sig_x"].reshape(1, -1), rng.uniform(-30, 30, (2048, 2048)).astype(np.float32),
+              rng.uniform(-104, 89, (512, 1024)).astype(np.float32)):
+        got = run_unary(ttc, ttc.OP_SIGMOID, x)
+        d_cr = ulp_dist(got, oracle.sigmoid_cr(x))
+        assert d_cr.max() <= 1, d_cr.max()
+        d = ulp_dist(got, oracle.sigmoid(x))
+        assert d.max() <= 3, d.max()
+        assert np.mean(d > 2) < 1e-3
+    got = run_unary(ttc, ttc.OP_SIGMOID, golden["sig_x"].reshape(1, -1))
+    assert ulp_dist(got.ravel(), golden["sig_y"]).max() <= 3
 
 
 @pytest.mark.parametrize("shape", SHAPES)

@@ -37,7 +37,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC",
                      "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
 
-CUDA_SOURCES = ["runtime.cu", "chain.cu", "transpose.cu", "gemm_ffma.cu", "gemm_tc.cu"]
+CUDA_SOURCES = ["runtime.cu", "chain.cu", "chain_tma.cu", "transpose.cu", "gemm_ffma.cu", "gemm_tc.cu"]
 CPP_SOURCES = ["comm.cpp"]
 
 

@@ -11,11 +11,15 @@
 // iterate grid-stride. Compiled with -fmad=false: each step is a single IEEE
 // op, as in the reference's separate passes.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 
-#include "ttc_internal.cuh"
+#include "tma_util.cuh"
 
 namespace ttc {
+
+// Staged (TMA-fed) variant, chain_tma.cu: launches when the layout allows it.
+int launch_chain_tma(const ttc_chain_desc& d, const DProgram& prog, bool* launched);
 
 namespace {
 
@@ -39,6 +43,10 @@ struct ChainParams {
 template <int W, bool REDUCE_ALL>
 __global__ void __launch_bounds__(kThreads) chain_flat_kernel(const __grid_constant__ ChainParams p) {
     constexpr int G = kGroups;
+    if (p.prog.has_sigmoid) {
+        exp2_table_init_block();
+        __syncthreads();
+    }
     const long long seg = blockIdx.y;
     float sum = 0.0f;
     for (unsigned blk = blockIdx.x; (unsigned long long)blk * (kThreads * G) < p.total; blk += gridDim.x) {
@@ -81,6 +89,10 @@ __global__ void __launch_bounds__(kThreads) chain_flat_kernel(const __grid_const
 template <int W>
 __global__ void __launch_bounds__(kThreads) chain_rows_kernel(const __grid_constant__ ChainParams p) {
     constexpr int G = kGroups;
+    if (p.prog.has_sigmoid) {
+        exp2_table_init_block();
+        __syncthreads();
+    }
     const long long seg = blockIdx.y;
     const int lane = threadIdx.x & 31;
     const unsigned warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
@@ -120,6 +132,10 @@ template <int W>
 __global__ void __launch_bounds__(kThreads) chain_cols_kernel(const __grid_constant__ ChainParams p) {
     constexpr int G = kGroups;
     constexpr int NW = kThreads / 32;
+    if (p.prog.has_sigmoid) {
+        exp2_table_init_block();
+        __syncthreads();
+    }
     const long long seg = blockIdx.z;
     const int split = blockIdx.y;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -290,6 +306,18 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p) {
 
 }  // namespace
 
+void launch_finalize_all(const float* partials, int nparts, float* out, int mean, double count) {
+    finalize_all_kernel<<<1, 256, 0, rt().stream>>>(partials, nparts, out, 0, mean, count);
+    count_launch();
+}
+
+void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg, float* out, long long sseg, int mean,
+                          double count) {
+    finalize_cols_kernel<<<dim3((cols + 255) / 256, nseg), 256, 0, rt().stream>>>(partials, nsplit, cols, out, sseg,
+                                                                                   mean, count);
+    count_launch();
+}
+
 int run_chain(const ttc_chain_desc& d) {
     if (d.rows < 0 || d.cols < 0 || d.nseg < 1)
         return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: chain shape rows=%d cols=%d nseg=%d is invalid", d.rows,
@@ -322,6 +350,15 @@ int run_chain(const ttc_chain_desc& d) {
             return check_cuda(cudaGetLastError(), "fill kernel launch");
         }
         return TTC_OK;
+    }
+    static const bool tma_enabled = [] {
+        const char* e = getenv("TTC_CHAIN_TMA");
+        return !(e && e[0] == '0');
+    }();
+    if (tma_enabled) {
+        bool launched = false;
+        if (int rc = launch_chain_tma(d, p.prog, &launched)) return rc;
+        if (launched) return TTC_OK;
     }
     const bool vec = vector_ok(d);
     const int W = vec ? 4 : 1;

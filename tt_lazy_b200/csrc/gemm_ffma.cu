@@ -39,6 +39,10 @@ template <bool TA, bool TB, bool VEC>
 __global__ void __launch_bounds__(kThreads) sgemm_kernel(const __grid_constant__ GemmParams p) {
     __shared__ __align__(16) float As[2][BK][BM + 4];
     __shared__ __align__(16) float Bs[2][BK][BN + 4];
+    if (p.epi.has_sigmoid) {
+        exp2_table_init_block();
+        __syncthreads();
+    }
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     float acc[8][8];

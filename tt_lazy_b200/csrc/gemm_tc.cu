@@ -26,15 +26,11 @@
 // a multi-GPU run. Every mbarrier wait is bounded (about 2 s); an expired
 // wait records an error in a host-mapped status word, lets the other roles
 // time out too, waits for its own TMA loads, frees TMEM and returns.
-#include <cuda.h>
-
 #include <cstring>
 
-#include "ttc_internal.cuh"
+#include "tma_util.cuh"
 
 namespace ttc {
-
-int device_status_ptr(int** dptr);
 
 namespace {
 
@@ -45,7 +41,6 @@ constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int kThreads = 192;
 constexpr int GROUP_M = 16;
-constexpr long long kWaitLimit = 4000000000ll;  // clock cycles (~2 s)
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
 
 struct TcParams {
@@ -58,45 +53,6 @@ struct TcParams {
     int* status;
     DProgram epi;
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}\n"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait for the phase with the given parity; false when it expired.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const long long t0 = clock64();
-    while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > kWaitLimit) return false;
-    return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
-            dst),
-        "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
-        : "memory");
-}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -128,16 +84,20 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Shared-memory matrix descriptor, 128-byte swizzle (sm_100 layout: start
-// address, leading / stride byte offsets in 16-byte units, version 1,
-// layout type 2 = SWIZZLE_128B).
-__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor (sm_100 layout: start address, leading /
+// stride byte offsets in 16-byte units, version 1, layout type in bits
+// 61-63). Layout 2 = 128-byte rows swizzled in 16-byte chunks over 8 rows
+// (K-major operands); layout 1 = 128-byte rows swizzled in 32-byte chunks
+// over 4 rows, the only layout tcgen05 accepts for MN-major 32-bit operands.
+constexpr uint32_t kLayoutSW128 = 2, kLayoutSW128Base32 = 1;
+__device__ __forceinline__ uint64_t make_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFF);
     d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
     d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;
-    d |= (uint64_t)2 << 61;
+    d |= (uint64_t)layout << 61;
     return d;
 }
 
@@ -173,9 +133,9 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             mbar_init(tfull_bar(b), 1);
             mbar_init(tempty_bar(b), 4);
         }
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_fence_init();
     }
+    if (p.epi.has_sigmoid) exp2_table_init_block();
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(TMEM_COLS)
@@ -239,8 +199,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16;
-            const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16;
+            // K-major: 8-row atoms of 1024 B (SBO), K advances 32 B per MMA
+            // inside the 128-byte row. MN-major: one TMA box of 32 rows x 128 B
+            // per 32 columns (LBO = box size), 4-row atoms of 512 B (SBO), K
+            // advances 8 rows = 1024 B per MMA.
+            const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16, a_sbo = p.a_mn_major ? 512 : 1024;
+            const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16, b_sbo = p.b_mn_major ? 512 : 1024;
+            const uint32_t a_lay = p.a_mn_major ? kLayoutSW128Base32 : kLayoutSW128;
+            const uint32_t b_lay = p.b_mn_major ? kLayoutSW128Base32 : kLayoutSW128;
             const uint32_t a_kstep = p.a_mn_major ? 8 * 128 : 32;
             const uint32_t b_kstep = p.b_mn_major ? 8 * 128 : 32;
             int stage = 0;
@@ -264,8 +230,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                     const uint32_t a_s = sbase + stage * STAGE_BYTES, b_s = a_s + A_BYTES;
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {
-                        const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, 1024);
-                        const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, 1024);
+                        const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, b_sbo, b_lay);
                         tc_mma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
                     }
                     tc_commit(empty_bar(stage));
@@ -330,41 +296,17 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                      : "memory");
 }
 
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-    static EncodeTiledFn fn = nullptr;
-    if (!fn) {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = (EncodeTiledFn)p;
-        else
-            cudaGetLastError();
-    }
-    return fn;
-}
-
 // 2-D fp32 tensor map over a row-major matrix with `outer` rows of `inner`
-// elements (row pitch ld elements), box {32, box_outer}, 128-byte swizzle,
-// out-of-bounds reads filled with zeros.
-int make_map(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld, int box_outer) {
-    EncodeTiledFn fn = encode_fn();
-    if (!fn) return set_error(TTC_ERR_CUDA, "tt_cuda: cuTensorMapEncodeTiled is unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
-    cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-    cuuint32_t box[2] = {32, (cuuint32_t)box_outer};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)ptr, dims, strides, box, estr,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS)
-        return set_error(TTC_ERR_CUDA, "tt_cuda: cuTensorMapEncodeTiled failed (%d) for %lld x %lld, ld %lld", (int)r,
-                         outer, inner, ld);
-    return TTC_OK;
+// elements (row pitch ld elements), box {32, box_outer}, out-of-bounds reads
+// filled with zeros. K-major tiles use the 16-byte-chunk 128-byte swizzle;
+// MN-major tiles the 32-byte-chunk one (matching descriptor layout 1).
+int make_map(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld, int box_outer,
+             bool mn_major) {
+    const unsigned long long dims[2] = {(unsigned long long)inner, (unsigned long long)outer};
+    const unsigned long long strides[1] = {(unsigned long long)ld};
+    const unsigned box[2] = {32, (unsigned)box_outer};
+    return encode_tensor_map_f32(map, ptr, 2, dims, strides, box,
+                                 mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace
@@ -391,15 +333,15 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi) {
     p.b_mn_major = d.trans_b ? 0 : 1;
     // A: logical [M, K]; K-major when stored [M, K] (trans_a = 0).
     if (!p.a_mn_major) {
-        if (int rc = make_map(&p.tma_a, d.a, d.K, d.M, d.lda, BM)) return rc;
+        if (int rc = make_map(&p.tma_a, d.a, d.K, d.M, d.lda, BM, false)) return rc;
     } else {
-        if (int rc = make_map(&p.tma_a, d.a, d.M, d.K, d.lda, BK)) return rc;
+        if (int rc = make_map(&p.tma_a, d.a, d.M, d.K, d.lda, BK, true)) return rc;
     }
     // B: logical [K, N]; MN-major when stored [K, N] (trans_b = 0).
     if (p.b_mn_major) {
-        if (int rc = make_map(&p.tma_b, d.b, d.N, d.K, d.ldb, BK)) return rc;
+        if (int rc = make_map(&p.tma_b, d.b, d.N, d.K, d.ldb, BK, true)) return rc;
     } else {
-        if (int rc = make_map(&p.tma_b, d.b, d.K, d.N, d.ldb, BN)) return rc;
+        if (int rc = make_map(&p.tma_b, d.b, d.K, d.N, d.ldb, BN, false)) return rc;
     }
     p.M = d.M;
     p.N = d.N;

@@ -7,7 +7,7 @@
 #include <cstring>
 #include <unordered_map>
 
-#include "ttc_internal.cuh"
+#include "tma_util.cuh"
 
 namespace ttc {
 
@@ -51,6 +51,41 @@ int workspace(size_t bytes, void** out) {
         r.workspace_bytes = want;
     }
     *out = r.workspace;
+    return TTC_OK;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tensor_map_f32(CUtensorMap* map, const void* ptr, int rank, const unsigned long long* dims,
+                          const unsigned long long* strides_elems, const unsigned* box, CUtensorMapSwizzle swizzle) {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+        else
+            cudaGetLastError();
+        if (!fn) return set_error(TTC_ERR_CUDA, "tt_cuda: cuTensorMapEncodeTiled is unavailable");
+    }
+    if (rank < 1 || rank > 5) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: tensor map rank %d", rank);
+    cuuint64_t d[5], s[4];
+    cuuint32_t b[5], e[5];
+    for (int i = 0; i < rank; ++i) {
+        d[i] = dims[i];
+        b[i] = box[i];
+        e[i] = 1;
+        if (i + 1 < rank) s[i] = strides_elems[i] * 4;
+    }
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, (cuuint32_t)rank, const_cast<void*>(ptr), d, s, b, e,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return set_error(TTC_ERR_CUDA, "tt_cuda: cuTensorMapEncodeTiled failed (%d): rank %d, dims %llu x %llu", (int)r,
+                         rank, (unsigned long long)d[0], rank > 1 ? (unsigned long long)d[1] : 1ull);
     return TTC_OK;
 }
 
@@ -142,6 +177,7 @@ int decode_program(const ttc_chain_desc& d, bool acc_preloaded, DProgram* out) {
             case TTC_OP_SIGMOID:
                 if (int rc = need_acc()) return rc;
                 op = in.op == TTC_OP_RELU ? D_RELU : D_SIGMOID;
+                if (op == D_SIGMOID) out->has_sigmoid = 1;
                 break;
             case TTC_OP_ADD:
             case TTC_OP_MUL: {
@@ -171,6 +207,7 @@ int decode_program(const ttc_chain_desc& d, bool acc_preloaded, DProgram* out) {
                     return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d saves to slot %d", pc, in.idx);
                 op = (uint8_t)(D_SAVE0 + in.idx);
                 slot_defined[in.idx] = true;
+                if (in.idx + 1 > out->n_slots) out->n_slots = in.idx + 1;
                 break;
             case TTC_OP_STORE:
                 if (int rc = need_acc()) return rc;

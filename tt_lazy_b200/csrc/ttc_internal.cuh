@@ -90,6 +90,8 @@ struct DOutView {
 struct DProgram {
     int n_instr;
     int n_in, n_out;
+    int has_sigmoid;  // kernels fill the exp table only when a step needs it
+    int n_slots;      // 1 + highest save slot the program uses (0 if none)
     uint8_t op[TTC_CHAIN_MAX_INSTR];
     uint8_t arg[TTC_CHAIN_MAX_INSTR];
     DInView in[TTC_CHAIN_MAX_INPUTS];
@@ -151,7 +153,41 @@ __device__ __forceinline__ void store_group(const DOutView& v, long long seg, lo
 }
 
 __device__ __forceinline__ float op_relu(float x) { return (0.0f < x) ? x : 0.0f; }
-__device__ __forceinline__ float op_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+// exp for the sigmoid step, rounded once from a double approximation with
+// relative error below 2^-44, so the float result is the correctly rounded
+// e^x except within 2^-44 of a rounding midpoint. The CPU reference gets
+// e^x from glibc's expf (within 0.502 ulp), so both sides nearly always hold
+// the same float and the IEEE add and divide that follow match bit for bit;
+// a 2-ulp expf would put sigmoid up to 4 ulp away.
+// Method: table-driven reduction (P. T. P. Tang, "Table-driven implementation
+// of the exponential function in IEEE floating-point arithmetic", ACM TOMS
+// 15(2), 1989): x = (64 m + j) ln2/64 + r with |r| <= ln2/128, e^x =
+// 2^m * 2^(j/64) * e^r, e^r by its degree-4 Taylor polynomial (truncation
+// error < 4e-14 on that interval). The 2^(j/64) table lives in shared memory
+// (exp2_table_init fills it at kernel start).
+static __shared__ double s_exp2_tab[64];
+
+__device__ __forceinline__ void exp2_table_init_block() {
+    for (int i = threadIdx.x; i < 64; i += blockDim.x) s_exp2_tab[i] = exp2((double)i * (1.0 / 64.0));
+}
+
+__device__ __forceinline__ float exp_rn(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return __int_as_float(0x7f800000);  // overflows to +inf
+    if (x < -104.0f) return 0.0f;                      // below half the smallest subnormal
+    const int k = __float2int_rn(x * 92.33248261689366f);  // x * 64 / ln2
+    const double r = fma(-(double)k, 0.010830424696249145, (double)x);  // x - k ln2/64
+    double p = fma(r, 1.0 / 24.0, 1.0 / 6.0);
+    p = fma(p, r, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    double e = p * s_exp2_tab[k & 63];
+    e = __longlong_as_double(__double_as_longlong(e) + (long long)(k >> 6) * (1ll << 52));  // * 2^m
+    return __double2float_rn(e);
+}
+
+__device__ __forceinline__ float op_sigmoid(float x) { return 1.0f / (1.0f + exp_rn(-x)); }
 
 // Applies f(g, w) to every element. Arithmetic runs on all groups (invalid
 // groups compute on zeros and are never stored or summed).
@@ -163,12 +199,33 @@ __device__ __forceinline__ void each(F&& f) {
         for (int w = 0; w < W; ++w) f(g, w);
 }
 
+// Memory policy of the interpreter: operands come straight from global
+// memory through the program's views. Other kernels supply their own policy
+// (the staged chain kernel reads full operands from shared memory).
 template <int G, int W>
-__device__ __forceinline__ void run_program(const DProgram& P, float (&acc)[G][W], long long seg,
-                                            const long long (&row)[G], const long long (&col)[G],
-                                            const bool (&valid)[G]) {
-    float s0[G][W], s1[G][W], s2[G][W], s3[G][W];
-    each<G, W>([&](int g, int w) { s0[g][w] = s1[g][w] = s2[g][w] = s3[g][w] = 0.0f; });
+struct GlobalIO {
+    const DProgram& P;
+    long long seg;
+    const long long (&row)[G];
+    const long long (&col)[G];
+    const bool (&valid)[G];
+    __device__ __forceinline__ bool ok(int g) const { return valid[g]; }
+    __device__ __forceinline__ void load(int k, int g, float (&dst)[W]) const {
+        load_group<W>(P.in[k], seg, row[g], col[g], dst);
+    }
+    __device__ __forceinline__ void store(int j, int g, const float (&src)[W]) const {
+        store_group<W>(P.out[j], seg, row[g], col[g], src);
+    }
+};
+
+// Runs the program on acc. NS = save slots the caller's programs may use
+// (slots >= NS never occur: the host picks the instantiation from the
+// decoded program), so unused slots cost no registers.
+template <int G, int W, int NS, class IO>
+__device__ __forceinline__ void run_program_io(const DProgram& P, float (&acc)[G][W], const IO& io) {
+    float s[NS][G][W];
+#pragma unroll
+    for (int k = 0; k < NS; ++k) each<G, W>([&](int g, int w) { s[k][g][w] = 0.0f; });
 
     for (int pc = 0; pc < P.n_instr; ++pc) {
         const int a = P.arg[pc];
@@ -176,51 +233,57 @@ __device__ __forceinline__ void run_program(const DProgram& P, float (&acc)[G][W
             case D_LOAD:
 #pragma unroll
                 for (int g = 0; g < G; ++g)
-                    if (valid[g]) load_group<W>(P.in[a], seg, row[g], col[g], acc[g]);
+                    if (io.ok(g)) io.load(a, g, acc[g]);
                 break;
             case D_RELU: each<G, W>([&](int g, int w) { acc[g][w] = op_relu(acc[g][w]); }); break;
             case D_SIGMOID: each<G, W>([&](int g, int w) { acc[g][w] = op_sigmoid(acc[g][w]); }); break;
             case D_ADD_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + acc[g][w]; }); break;
             case D_MUL_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * acc[g][w]; }); break;
-            case D_ADD_IN: {
-                float t[G][W];
-                each<G, W>([&](int g, int w) { t[g][w] = 0.0f; });
-#pragma unroll
-                for (int g = 0; g < G; ++g)
-                    if (valid[g]) load_group<W>(P.in[a], seg, row[g], col[g], t[g]);
-                each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + t[g][w]; });
-                break;
-            }
+            case D_ADD_IN:
             case D_MUL_IN: {
                 float t[G][W];
                 each<G, W>([&](int g, int w) { t[g][w] = 0.0f; });
 #pragma unroll
                 for (int g = 0; g < G; ++g)
-                    if (valid[g]) load_group<W>(P.in[a], seg, row[g], col[g], t[g]);
-                each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * t[g][w]; });
+                    if (io.ok(g)) io.load(a, g, t[g]);
+                if (P.op[pc] == D_ADD_IN)
+                    each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + t[g][w]; });
+                else
+                    each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * t[g][w]; });
                 break;
             }
-            case D_ADD_S0: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s0[g][w]; }); break;
-            case D_ADD_S1: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s1[g][w]; }); break;
-            case D_ADD_S2: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s2[g][w]; }); break;
-            case D_ADD_S3: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s3[g][w]; }); break;
-            case D_MUL_S0: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s0[g][w]; }); break;
-            case D_MUL_S1: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s1[g][w]; }); break;
-            case D_MUL_S2: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s2[g][w]; }); break;
-            case D_MUL_S3: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s3[g][w]; }); break;
-            case D_SAVE0: each<G, W>([&](int g, int w) { s0[g][w] = acc[g][w]; }); break;
-            case D_SAVE1: each<G, W>([&](int g, int w) { s1[g][w] = acc[g][w]; }); break;
-            case D_SAVE2: each<G, W>([&](int g, int w) { s2[g][w] = acc[g][w]; }); break;
-            case D_SAVE3: each<G, W>([&](int g, int w) { s3[g][w] = acc[g][w]; }); break;
+#define TTC_SLOT_CASES(K)                                                                                 \
+    case D_ADD_S0 + K:                                                                                    \
+        if constexpr (NS > K) each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + s[K % NS][g][w]; }); \
+        break;                                                                                            \
+    case D_MUL_S0 + K:                                                                                    \
+        if constexpr (NS > K) each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * s[K % NS][g][w]; }); \
+        break;                                                                                            \
+    case D_SAVE0 + K:                                                                                     \
+        if constexpr (NS > K) each<G, W>([&](int g, int w) { s[K % NS][g][w] = acc[g][w]; });             \
+        break;
+                TTC_SLOT_CASES(0)
+                TTC_SLOT_CASES(1)
+                TTC_SLOT_CASES(2)
+                TTC_SLOT_CASES(3)
+#undef TTC_SLOT_CASES
             case D_STORE:
 #pragma unroll
                 for (int g = 0; g < G; ++g)
-                    if (valid[g]) store_group<W>(P.out[a], seg, row[g], col[g], acc[g]);
+                    if (io.ok(g)) io.store(a, g, acc[g]);
                 break;
             default:
                 break;
         }
     }
+}
+
+template <int G, int W, int NS = 4>
+__device__ __forceinline__ void run_program(const DProgram& P, float (&acc)[G][W], long long seg,
+                                            const long long (&row)[G], const long long (&col)[G],
+                                            const bool (&valid)[G]) {
+    const GlobalIO<G, W> io{P, seg, row, col, valid};
+    run_program_io<G, W, NS>(P, acc, io);
 }
 
 // Warp / block sums used by the reductions (fixed shuffle order: the result
