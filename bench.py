@@ -1,0 +1,420 @@
+"""Benchmark of the tt_lazy B200 backend on its headline workloads.
+
+Headline (metric "fused-MLP TFLOP/s"): the large fp32 MLP, batch-sharded over
+the GPUs of one node -- X[65536, 4096] ~ N(0,1), W1[4096, 16384] and
+W2[16384, 4096] ~ N(0, 1/fan_in) (seed 2, synthetic), Y = sigmoid(relu(X W1)
+W2), s = reduce_sum(Y, dim 0) all-reduced across ranks. One step is one
+evaluation of that graph through the public front end (a compiled tape:
+two tcgen05 TF32 GEMMs with fused relu / sigmoid epilogues, the column
+reduction, the NCCL all-reduce when N > 1). The global batch is fixed (strong
+scaling); each rank holds 65536/N rows and a full copy of the weights.
+
+Beside it, in the same JSON line: the bandwidth graph (A[16384, 16384] ~
+U(-1,1), seed 3: transpose -> 8 column chunks -> sigmoid(C) * relu(C + C) ->
+reduce_sum dim 1) as "eltwise_chain" in HBM GB/s, the roofline of the
+dominant kernel, a CPU baseline (the reference's own code, compiled from its
+sources, on a row sample), the end-to-end number through the public API with
+host buffers, and the SM clocks seen while timing.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+M_GLOBAL, K1, N1 = 65536, 4096, 16384
+FLOP_STEP = 2 * M_GLOBAL * K1 * N1 * 2  # two GEMMs: 1.759e13
+CHAIN_N, CHAIN_SPLIT = 16384, 2048
+CHAIN_BYTES = CHAIN_N * CHAIN_N * 4 + 8 * CHAIN_N * 4
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons while timing."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.Q,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+                self.lines = [l for l in out.splitlines() if l.strip()]
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ helpers
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def pinned(shape, capi):
+    """numpy view of pinned host memory (fast H2D for the end-to-end run)."""
+    n = int(np.prod(shape))
+    p = C.c_void_p()
+    capi.check(capi.lib().ttc_host_alloc(n * 4, C.byref(p)))
+    buf = (C.c_float * n).from_address(p.value)
+    return np.ctypeslib.as_array(buf).reshape(shape), p.value
+
+
+def make_inputs(rank, world):
+    rng = np.random.default_rng(2)
+    W1 = (rng.standard_normal((K1, N1), dtype=np.float32) / np.float32(np.sqrt(K1)))
+    W2 = (rng.standard_normal((N1, K1), dtype=np.float32) / np.float32(np.sqrt(N1)))
+    rows = M_GLOBAL // world
+    xr = np.random.default_rng(1000 + 2 * 97 + rank)  # seed 2, one stream per shard
+    X = xr.standard_normal((rows, K1), dtype=np.float32)
+    return X, W1, W2
+
+
+# ------------------------------------------------------------- CPU baseline
+def cpu_reference_rate(X, W1, W2, threads, seconds_target=12.0, rows_per_call=8):
+    """TFLOP/s of the reference's own CPU code (oracle/_ref) on a row sample."""
+    import oracle
+
+    R = oracle.Ref()
+    L = R.L
+    w1s = np.asarray(W1.shape, np.uint32)
+    w2s = np.asarray(W2.shape, np.uint32)
+    rc = L.ref_mlp_prepare(W1.ctypes.data_as(C.c_void_p), w1s.ctypes.data_as(C.c_void_p),
+                           W2.ctypes.data_as(C.c_void_p), w2s.ctypes.data_as(C.c_void_p))
+    if rc != 0:
+        raise RuntimeError(L.ref_last_error().decode())
+    flop_row = 2 * K1 * N1 * 2
+    done = [0] * threads
+    stop = time.perf_counter() + seconds_target
+
+    def work(t):
+        out = np.empty(K1, np.float32)
+        r0 = (t * rows_per_call * 97) % (X.shape[0] - rows_per_call)
+        while time.perf_counter() < stop:
+            xs = np.ascontiguousarray(X[r0:r0 + rows_per_call])
+            rc = L.ref_mlp_rows(xs.ctypes.data_as(C.c_void_p), C.c_uint32(rows_per_call), C.c_uint32(K1),
+                                out.ctypes.data_as(C.c_void_p))
+            if rc != 0:
+                raise RuntimeError(L.ref_last_error().decode())
+            done[t] += rows_per_call
+            r0 = (r0 + rows_per_call * threads) % (X.shape[0] - rows_per_call)
+
+    t0 = time.perf_counter()
+    ths = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    dt = time.perf_counter() - t0
+    rows = sum(done)
+    return rows * flop_row / dt / 1e12, rows, dt
+
+
+def run_reference(args):
+    world, rank, local = dist_env()
+    if rank != 0:
+        return
+    import oracle
+
+    if oracle.ref() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libttref.so was not built"}))
+        return
+    X, W1, W2 = make_inputs(0, 1)
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, rows, dt = cpu_reference_rate(X, W1, W2, threads, seconds_target=args.ref_seconds)
+        if i >= args.warmup:
+            vals.append((v, rows, dt))
+    v = statistics.median([x[0] for x in vals])
+    sample = f"{vals[-1][1]} rows of X per step ({threads} threads x 8-row calls, ~{args.ref_seconds:.0f} s), " \
+             f"extrapolated to the full 65536-row step"
+    line = {
+        "metric": "fused-MLP TFLOP/s", "value": v, "unit": "TFLOP/s", "impl": "reference",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": FLOP_STEP / (v * 1e12) * 1e3, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1) inputs, N(0,1/fan_in) weights)",
+        "config": {"workload": "large fp32 MLP X[65536,4096] W1[4096,16384] W2[16384,4096] relu->sigmoid, "
+                               "reduce_sum over batch, seed 2", "global_batch": M_GLOBAL, "parallelism": "cpu"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+
+    world, rank, local = dist_env()
+    os.environ.setdefault("TT_LAZY_DEVICE", str(local))
+    torch.cuda.set_device(local)
+    import tt_lazy_b200 as tl
+    from tt_lazy_b200 import capi
+
+    tl.backend_init()
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        uid = tl.comm_unique_id() if rank == 0 else None
+        obj = [uid]
+        dist.broadcast_object_list(obj, src=0)
+        tl.comm_init(world, rank, obj[0], 60000)
+    stream = torch.cuda.ExternalStream(tl.stream())
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    X, W1, W2 = make_inputs(rank, world)
+    rows = X.shape[0]
+
+    def graph(xt):
+        h = tl.relu(tl.matmul(xt, tl.constant(W1)))
+        y = tl.sigmoid(tl.matmul(h, tl.constant(W2)))
+        s = tl.reduce_sum(y, [0])
+        return tl.all_reduce_sum(s) if world > 1 else s
+
+    # ---- device-resident inputs: the hot path alone
+    s_dev = graph(tl.constant(X))
+    plan = tl.Plan([s_dev])
+    for _ in range(args.warmup):
+        plan.run()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        barrier()
+        e0.record(stream)
+        for _ in range(args.steps):
+            plan.run()
+        e1.record(stream)
+        barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    launches = plan.kernels_last_run * args.steps
+    value = FLOP_STEP / (ms * 1e-3) / 1e12
+    s_val = plan.numpy(0)
+    assert np.all(np.isfinite(s_val)), "non-finite result"
+
+    # ---- end to end through the public API with host buffers
+    Xp, _ = pinned(X.shape, capi)
+    Xp[...] = X
+    s_e2e = graph(tl.streamed(Xp))
+    plan_e2e = tl.Plan([s_e2e])
+    for _ in range(max(1, args.warmup - 1)):
+        plan_e2e.run()
+        plan_e2e.numpy(0)
+    barrier()
+    t0 = time.perf_counter()
+    e2 = torch.cuda.Event(enable_timing=True)
+    e3 = torch.cuda.Event(enable_timing=True)
+    e2.record(stream)
+    for _ in range(args.steps):
+        plan_e2e.run()
+        out = plan_e2e.numpy(0)  # the device -> host read of the step's result
+    e3.record(stream)
+    barrier()
+    ms_e2e = max_over_ranks(max(e2.elapsed_time(e3), (time.perf_counter() - t0) * 1e3) / args.steps)
+    e2e_value = FLOP_STEP / (ms_e2e * 1e-3) / 1e12
+    del plan_e2e, s_e2e
+
+    # ---- roofline of the dominant kernel: the first GEMM (TF32 tcgen05) timed alone
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    tf32_peak = bf16_peak / 2.0
+    Xd = capi.DeviceArray.from_numpy(X[: min(rows, 16384)])
+    W1d = capi.DeviceArray.from_numpy(W1)
+    Hd = capi.DeviceArray.empty((Xd.shape[0], N1))
+    capi.check(capi.lib().ttc_set_stream(C.c_void_p(tl.stream())))
+    Mg = Xd.shape[0]
+
+    def one_gemm():
+        capi.gemm(Mg, N1, K1, Xd.ptr, K1, W1d.ptr, N1, Hd.ptr, N1, path=capi.GEMM_TF32)
+
+    for _ in range(3):
+        one_gemm()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record(stream)
+    reps = 10
+    for _ in range(reps):
+        one_gemm()
+    g1.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = g0.elapsed_time(g1) / reps
+    gemm_tflops = 2 * Mg * N1 * K1 / (gemm_ms * 1e-3) / 1e12
+    launches += reps + 3
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "tf32_gemm_traffic.txt")
+    if os.path.exists(tp):
+        try:
+            per_flop = float(open(tp).read().split("bytes_per_flop=")[1].split()[0])
+            traffic = per_flop * 2 * Mg * N1 * K1
+        except Exception:
+            traffic = None
+    del Xd, W1d, Hd
+
+    # ---- bandwidth graph (eltwise chain block)
+    chain = None
+    if not args.skip_chain:
+        rng = np.random.default_rng(3)
+        A = rng.uniform(-1, 1, (CHAIN_N, CHAIN_N)).astype(np.float32)
+        T = tl.transpose(tl.constant(A))
+        outs = [tl.reduce_sum(tl.multiply(tl.sigmoid(ch), tl.relu(tl.add(ch, ch))), [1])
+                for ch in tl.split(T, CHAIN_SPLIT, 1)]
+        cplan = tl.Plan(outs)
+        for _ in range(3):
+            cplan.run()
+        barrier()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        creps = 20
+        c0.record(stream)
+        for _ in range(creps):
+            cplan.run()
+        c1.record(stream)
+        barrier()
+        cms = max_over_ranks(c0.elapsed_time(c1) / creps)
+        gbs = CHAIN_BYTES / (cms * 1e-3) / 1e9
+        launches += cplan.kernels_last_run * (creps + 3)
+        chain = {"metric": "eltwise-chain HBM GB/s", "value": gbs * world, "unit": "GB/s", "per_gpu": gbs,
+                 "ms_per_step": cms, "kernels_per_step": cplan.kernels_last_run,
+                 "workload": "A[16384,16384] U(-1,1) seed 3: transpose -> 8 column chunks -> "
+                             "sigmoid(C)*relu(C+C) -> reduce_sum dim 1 (replica per GPU)",
+                 "algorithmic_bytes": CHAIN_BYTES,
+                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
+                              "frac": gbs / hbm_peak, "peak_source": peak_kind}}
+        del cplan, outs
+
+    # ---- CPU baseline (rank 0, N = 1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.skip_cpu:
+        try:
+            v, nrows, dt = cpu_reference_rate(X, W1, W2, threads=1, seconds_target=args.ref_seconds)
+            cpu = {"value": v, "unit": "TFLOP/s", "cores": 1, "kind": "reference",
+                   "sample": f"{nrows} rows of X through the reference's math::matmul/relu in {dt:.1f} s "
+                             f"(1 thread of {os.cpu_count()}), extrapolated to 65536 rows"}
+        except Exception as e:  # noqa: BLE001
+            cpu = {"value": None, "unit": "TFLOP/s", "cores": 0, "kind": "reference", "sample": f"failed: {e}"}
+
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": "fused-MLP TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32 (tf32 tensor-core GEMM, fp32 accumulate)",
+            "data": "synthetic (seeded N(0,1) inputs, N(0,1/fan_in) weights)",
+            "config": {"workload": "large fp32 MLP X[65536,4096] W1[4096,16384] W2[16384,4096] relu->sigmoid, "
+                                   "reduce_sum over batch, all-reduced; seed 2",
+                       "global_batch": M_GLOBAL, "rows_per_gpu": rows, "parallelism": f"dp{world} (batch-sharded)",
+                       "l2": "inputs larger than L2 (X shard >= 128 MiB, W1/W2 256 MiB)"},
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
+                    "h2d_bytes_per_step": int(X.nbytes), "d2h_bytes_per_step": int(K1 * 4),
+                    "path": "tt_lazy Plan.run() over a streamed pinned-host X + to-host read of s"},
+            "roofline": {"bound": "tensor", "kernel": "tf32_gemm_kernel (tcgen05, 128x256 tiles)",
+                         "achieved": gemm_tflops, "peak": tf32_peak, "unit": "TFLOP/s",
+                         "frac": gemm_tflops / tf32_peak, "traffic": traffic,
+                         "peak_source": f"{peak_kind} bf16 dense / 2 (TF32 rate)",
+                         "launch_ms": gemm_ms, "shape": [Mg, N1, K1]},
+            "eltwise_chain": chain,
+            "cpu_baseline": cpu,
+            "gpu_launches": int(launches),
+            "clocks": clocks,
+            "checksum": float(np.sum(s_val, dtype=np.float64)),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        tl.comm_destroy()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--skip-chain", action="store_true")
+    ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--ref-seconds", type=float, default=12.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        # keep the whole reference run within a few minutes
+        args.ref_seconds = min(args.ref_seconds, 150.0 / (args.steps + args.warmup))
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -97,7 +97,7 @@ int ttc_get_memory_stats(ttc_memory_stats* out);
  *
  * The program is an accumulator machine: `acc` holds the current value,
  * four save slots hold intermediates.
- *   LOAD  k      acc = input[k]
+ *   LOAD  k      acc = input[k]       (src = SLOT: acc = slot[k])
  *   RELU         acc = (0.0f < acc) ? acc : 0.0f         (std::max(0.0f, x))
  *   SIGMOID      acc = 1.0f / (1.0f + expf(-acc))
  *   ADD  src     acc = acc + src     src = ACC | INPUT k | SLOT s

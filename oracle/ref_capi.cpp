@@ -19,6 +19,7 @@
 #include "math_operations.hpp"
 #include "operations.hpp"
 
+#include <cmath>
 #include <cstring>
 #include <stdexcept>
 #include <string>
@@ -179,6 +180,42 @@ int ref_lazy_fused_mlp(const float* x, const uint32_t* xs, const float* w, const
         auto v = y.to_vector();
         std::memcpy(out, v.data(), v.size() * sizeof(float));
         fresh_graph();
+    });
+}
+
+// ---- timed CPU baseline of the large MLP workload (bench.py --impl reference)
+// Y = sigmoid(relu(X W1) W2), s = column sums of Y, for a row sample of X.
+// The two matmuls and the relu are the reference's own math::matmul /
+// math::relu (src/backend/cpu/matmul.cpp, eltwise.cpp); the reference has no
+// sigmoid and no per-dim reduction on this path, so those two cheap steps
+// follow the README formula (README.md:332) and a sequential column sum.
+// Weights are wrapped once (ref_mlp_prepare) so every call times only the
+// compute; calls on different rows may run concurrently.
+namespace {
+Tensor* g_w1 = nullptr;
+Tensor* g_w2 = nullptr;
+}  // namespace
+
+int ref_mlp_prepare(const float* w1, const uint32_t* w1s, const float* w2, const uint32_t* w2s) {
+    return guarded([&] {
+        delete g_w1;
+        delete g_w2;
+        g_w1 = new Tensor(materialized(w1, w1s, 2));
+        g_w2 = new Tensor(materialized(w2, w2s, 2));
+    });
+}
+
+int ref_mlp_rows(const float* x, uint32_t rows, uint32_t k, float* colsum) {
+    return guarded([&] {
+        if (!g_w1 || !g_w2) throw std::runtime_error("ref_mlp_prepare not called");
+        uint32_t xs[2] = {rows, k};
+        Tensor h = math::relu(math::matmul(materialized(x, xs, 2), *g_w1));
+        Tensor y = math::matmul(h, *g_w2);
+        const float* yd = y.const_data_ptr();
+        const uint32_t n = y.size(1);
+        for (uint32_t j = 0; j < n; ++j) colsum[j] = 0.0f;
+        for (uint32_t i = 0; i < rows; ++i)
+            for (uint32_t j = 0; j < n; ++j) colsum[j] += 1.0f / (1.0f + std::exp(-yd[(size_t)i * n + j]));
     });
 }
 

@@ -1,0 +1,133 @@
+"""Front end on the CPU: graph building, shapes and errors (the reference's
+graph-only unit / integration tests, tests/cpp/unit/*, tests/cpp/integration/
+test_operations.cpp), tape generation, dead-code elimination and what the
+fusion passes make of each workload's graph. Nothing here evaluates."""
+import numpy as np
+import pytest
+
+import tt_lazy_b200 as tl
+
+
+@pytest.fixture(autouse=True)
+def fresh():
+    tl.clear()
+    yield
+    tl.clear()
+
+
+def c(shape, seed=0):
+    return tl.constant(np.random.default_rng(seed).uniform(-1, 1, shape).astype(np.float32))
+
+
+def test_lazy_shapes_keep_true_rank():
+    x = c((2, 4))
+    y = tl.relu(x)
+    assert y.is_lazy and not y.is_evaluated
+    assert y.shape == [2, 4] and y.rank == 2
+    assert tl.matmul(x, c((4, 3))).shape == [2, 3]
+    assert tl.matmul(x, c((2, 3)), transpose_a=True).shape == [4, 3]
+    assert tl.transpose(x).shape == [4, 2]
+    assert tl.reduce_sum(x).shape == [1]
+    assert tl.reduce_sum(x, [1]).shape == [2]
+    assert tl.reduce_mean(x, [0], True).shape == [1, 4]
+    parts = tl.split(c((10, 3)), 4, 0)
+    assert [p.shape for p in parts] == [[4, 3], [4, 3], [2, 3]]
+    assert [p.output_index for p in parts] == [0, 1, 2]
+    assert tl.add(c((3, 5)), c((1, 5))).shape == [3, 5]
+    assert tl.fused_mlp(x, c((4, 8)), c((1, 8))).shape == [2, 8]
+
+
+def test_shape_errors_carry_reference_messages():
+    with pytest.raises(RuntimeError, match="Broadcasting addition not implemented"):
+        tl.add(c((3, 5)), c((3, 1)))
+    with pytest.raises(RuntimeError, match="Broadcasting multiplication not fully implemented"):
+        tl.multiply(c((3, 5)), c((1, 5)))
+    with pytest.raises(RuntimeError, match="Matrix dimension mismatch"):
+        tl.matmul(c((3, 5)), c((3, 5)))
+    with pytest.raises(RuntimeError, match="Split size must be positive"):
+        tl.split(c((4,)), 0)
+    with pytest.raises(RuntimeError, match="Transpose requires at least 2D"):
+        tl.transpose(c((4,)))
+
+
+def ops(outs):
+    return [o["op"] for o in tl.tape(outs)]
+
+
+def test_readme_chain_fuses_to_one_kernel_with_tail_sum():
+    x = c((1000, 1000))
+    y = tl.relu(x)
+    z = tl.add(y, y)
+    w = tl.multiply(z, z)
+    s = tl.reduce_sum(w)
+    t = tl.tape([w, s])
+    assert len(t) == 1
+    assert t[0]["op"] == "FusedChain[relu -> add -> multiply -> reduce]"
+    assert sorted(t[0]["outputs"]) == sorted([w.producer_node, s.producer_node])
+
+
+def test_mlp_fusion_absorbs_bias_and_activation():
+    X, W1, b1, W2, b2 = c((256, 512)), c((512, 1024)), c((1, 1024)), c((1024, 512)), c((1, 512))
+    h = tl.relu(tl.add(tl.matmul(X, W1), b1))
+    y = tl.add(tl.matmul(h, W2), b2)
+    m = tl.reduce_mean(y, [0])
+    assert ops([m]) == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add]", "Reduce"]
+    # an intermediate requested as an output is not absorbed
+    assert ops([m, h])[:2] == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add]"]
+    tl.set_optimization(False)
+    try:
+        assert ops([m]) == ["MatMul", "Add", "ReLU", "MatMul", "Add", "Reduce"]
+    finally:
+        tl.set_optimization(True)
+
+
+def test_large_mlp_sigmoid_then_batch_sum():
+    X, W1, W2 = c((64, 32)), c((32, 128)), c((128, 32))
+    y = tl.sigmoid(tl.matmul(tl.relu(tl.matmul(X, W1)), W2))
+    s = tl.reduce_sum(y, [0])
+    assert ops([s]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid]", "Reduce"]
+
+
+def test_bandwidth_graph_views_and_chains():
+    A = c((64, 64))
+    T = tl.transpose(A)
+    chunks = tl.split(T, 8, 1)
+    outs = []
+    for ch in chunks:
+        y = tl.multiply(tl.sigmoid(ch), tl.relu(tl.add(ch, ch)))
+        outs.append(tl.reduce_sum(y, [1]))
+    t = ops(outs)
+    assert t[:2] == ["Transpose", "Split"]
+    assert t[2:] == ["FusedChain[sigmoid -> add -> relu -> multiply -> reduce]"] * 8
+
+
+def test_dead_code_is_not_on_the_tape():
+    x = c((8, 8))
+    live = tl.relu(x)
+    for _ in range(5):
+        tl.sigmoid(tl.add(x, x))  # unreachable from `live`
+    assert tl.graph_size() == 11
+    t = tl.tape([live])
+    assert len(t) == 1 and t[0]["op"].startswith("FusedChain[relu")
+
+
+def test_random_dag_fusion_is_acyclic_and_complete():
+    rng = np.random.default_rng(4)
+    vals = [c((16, 16), i) for i in range(4)]
+    nodes = []
+    for i in range(120):
+        kind = rng.integers(0, 5)
+        a = vals[rng.integers(0, len(vals))]
+        b = vals[rng.integers(0, len(vals))]
+        v = [tl.relu, tl.sigmoid][kind % 2](a) if kind < 2 else \
+            [tl.add, tl.multiply, lambda p, q: tl.matmul(p, q)][kind - 2](a, b)
+        vals.append(v)
+        nodes.append(v)
+    outs = [tl.reduce_sum(v) for v in nodes[-5:]]
+    t = tl.tape(outs)
+    produced = set()
+    for op in t:
+        for i in op["inputs"]:
+            assert i in produced, "operation reads a result produced later"
+        produced.update(op["outputs"])
+        produced.add(op["node"])

@@ -1,0 +1,205 @@
+"""End-to-end through the public front end (lazy graph -> tape -> fused
+sm_100a kernels -> to_numpy), against the CPU oracle and the reference's own
+known answers. Bounds as in test_kernels_gpu.py."""
+import numpy as np
+import pytest
+
+import oracle
+import tt_lazy_b200 as tl
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def fresh():
+    tl.clear()
+    tl.set_gemm_path("auto")
+    yield
+    tl.clear()
+
+
+def normwise(got, want):
+    w = want.astype(np.float64)
+    return np.linalg.norm(got.astype(np.float64) - w) / max(np.linalg.norm(w), 1e-300)
+
+
+def test_reference_known_answers():
+    # test_end_to_end.cpp:58-89
+    r = tl.matmul(tl.constant(np.full((2, 2), 2, np.float32)), tl.constant(np.full((2, 2), 3, np.float32)))
+    assert r.is_lazy
+    assert np.all(r.numpy() == 12.0) and r.is_evaluated
+    # test_end_to_end.cpp:94-124
+    x = np.array([-2.0, -1.0, 0.0, 1.0, 2.0, -0.5, 0.5, -3.0], np.float32).reshape(2, 4)
+    assert tl.relu(tl.constant(x)).numpy().ravel().tolist() == [0, 0, 0, 1, 2, 0, 0.5, 0]
+    # test_mlp_demo.cpp:261-299
+    two, three = tl.constant(np.full((2, 3), 2, np.float32)), tl.constant(np.full((2, 3), 3, np.float32))
+    assert np.all(tl.add(two, three).numpy() == 5) and np.all(tl.multiply(two, three).numpy() == 6)
+
+
+def test_materialized_inputs_work():
+    # The reference drops materialized non-constant inputs (TapeGenerator.cpp:159-170).
+    x = np.arange(-3, 3, dtype=np.float32).reshape(2, 3)
+    assert np.array_equal(tl.relu(tl.materialized(x)).numpy(), oracle.relu(x))
+
+
+def test_readme_chain_public_api(golden):
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, (1000, 1000)).astype(np.float32)
+    X = tl.constant(x)
+    y = tl.relu(X)
+    z = tl.add(y, y)
+    w = tl.multiply(z, z)
+    s = tl.reduce_sum(w)
+    tl.evaluate([w, s])
+    st = tl.stats()
+    assert st["fused_operations"] == 1 and st["kernels_launched"] <= 3
+    wn = w.numpy()
+    ow = oracle.multiply(oracle.add(oracle.relu(x), oracle.relu(x)), oracle.add(oracle.relu(x), oracle.relu(x)))
+    assert np.array_equal(wn, ow)
+    exact = oracle.reduce(ow, f64=True)[0]
+    assert abs(s.numpy()[0] - exact) <= 1e-5 * abs(exact)
+    # the reference tape's own output (golden fixture)
+    c = golden["chain_x"]
+    C = tl.constant(c)
+    yc = tl.relu(C)
+    zc = tl.add(yc, yc)
+    assert np.array_equal(tl.multiply(zc, zc).numpy(), golden["chain_w"])
+
+
+@pytest.mark.parametrize("path,tol", [("ffma", 1e-5), ("tf32", 2e-3)])
+def test_two_layer_mlp_mean(path, tol, golden):
+    tl.set_gemm_path(path)
+    rng = np.random.default_rng(1)
+    X = rng.standard_normal((256, 512)).astype(np.float32)
+    W1 = (rng.standard_normal((512, 1024)) / np.sqrt(512)).astype(np.float32)
+    W2 = (rng.standard_normal((1024, 512)) / np.sqrt(1024)).astype(np.float32)
+    b1 = rng.uniform(-0.1, 0.1, (1, 1024)).astype(np.float32)
+    b2 = rng.uniform(-0.1, 0.1, (1, 512)).astype(np.float32)
+    h = tl.relu(tl.add(tl.matmul(tl.constant(X), tl.constant(W1)), tl.constant(b1)))
+    y = tl.add(tl.matmul(h, tl.constant(W2)), tl.constant(b2))
+    m = tl.reduce_mean(y, [0])
+    got_y, got_m = None, None
+    tl.evaluate([y, m])
+    got_y, got_m = y.numpy(), m.numpy()
+    ho = oracle.relu(oracle.add(oracle.matmul(X, W1), b1))
+    yo = oracle.add(oracle.matmul(ho, W2), b2)
+    assert normwise(got_y, yo) <= tol
+    mo = oracle.reduce(yo, (0,), mean=True, f64=True)
+    assert normwise(got_m, mo) <= tol
+    # the reference's lazy MLP (golden fixture) through the explicit path
+    g = golden
+    out = tl.add(tl.matmul(tl.relu(tl.add(tl.matmul(tl.constant(g["mlp2_x"]), tl.constant(g["mlp2_w1"])),
+                                          tl.constant(g["mlp2_b1"]))), tl.constant(g["mlp2_w2"])),
+                 tl.constant(g["mlp2_b2"]))
+    assert normwise(out.numpy(), g["mlp2_y"]) <= tol
+
+
+@pytest.mark.parametrize("has_relu", [True, False])
+def test_explicit_fused_mlp(has_relu, golden):
+    tl.set_gemm_path("ffma")
+    g = golden
+    y = tl.fused_mlp(tl.constant(g["mm_a"]), tl.constant(g["mlp_w"]), tl.constant(g["mlp_b"]), has_relu)
+    want = g["mlp_relu_y"] if has_relu else g["mlp_lin_y"]
+    assert normwise(y.numpy(), want) <= 1e-5
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_matmul_transpose_flags(ta, tb):
+    # handle_matmul in the reference drops transpose_a/b (OperationHandlers.cpp:61)
+    tl.set_gemm_path("ffma")
+    rng = np.random.default_rng(2)
+    a = rng.standard_normal((40, 24)).astype(np.float32)
+    b = rng.standard_normal((40, 24)).astype(np.float32) if (ta != tb) else rng.standard_normal((24, 40)).astype(np.float32)
+    A = a if not ta else np.ascontiguousarray(a.T)
+    B = b
+    if ta == 0 and tb == 0:
+        A, B = a, rng.standard_normal((24, 40)).astype(np.float32)
+    elif ta == 1 and tb == 0:
+        A, B = rng.standard_normal((24, 40)).astype(np.float32), rng.standard_normal((24, 32)).astype(np.float32)
+    elif ta == 0 and tb == 1:
+        A, B = rng.standard_normal((40, 24)).astype(np.float32), rng.standard_normal((32, 24)).astype(np.float32)
+    else:
+        A, B = rng.standard_normal((24, 40)).astype(np.float32), rng.standard_normal((32, 24)).astype(np.float32)
+    got = tl.matmul(tl.constant(A), tl.constant(B), bool(ta), bool(tb)).numpy()
+    assert normwise(got, oracle.matmul(A, B, ta, tb)) <= 1e-5
+
+
+def test_transpose_split_views_feed_fused_chains():
+    rng = np.random.default_rng(3)
+    a = rng.uniform(-1, 1, (512, 512)).astype(np.float32)
+    T = tl.transpose(tl.constant(a))
+    chunks = tl.split(T, 64, 1)
+    outs = [tl.reduce_sum(tl.multiply(tl.sigmoid(ch), tl.relu(tl.add(ch, ch))), [1]) for ch in chunks]
+    tl.evaluate(outs)
+    t = oracle.transpose(a)
+    for i, o in enumerate(outs):
+        ch = t[:, 64 * i:64 * (i + 1)]
+        y = oracle.multiply(oracle.sigmoid(np.ascontiguousarray(ch)), oracle.relu(oracle.add(ch, ch)))
+        want = oracle.reduce(y, (1,), f64=True)
+        assert np.allclose(o.numpy(), want, rtol=1e-5, atol=1e-6)
+    # materialising a transposed view and split chunks: bit-exact copies
+    assert np.array_equal(tl.transpose(tl.constant(a)).numpy(), t)
+    parts = tl.split(tl.constant(a), 100, 0)
+    tl.evaluate(parts)
+    for p, want in zip(parts, oracle.split(a, 100, 0)):
+        assert np.array_equal(p.numpy(), want)
+    cols = tl.split(tl.constant(a), 200, 1)
+    for p, want in zip(cols, oracle.split(a, 200, 1)):
+        assert np.array_equal(p.numpy(), want)
+
+
+@pytest.mark.parametrize("dims,keep", [([], False), ([0], False), ([1], True), ([0, 1], False), ([-1], False)])
+@pytest.mark.parametrize("mean", [False, True])
+def test_reduce_semantics(dims, keep, mean):
+    rng = np.random.default_rng(4)
+    x = rng.uniform(-1, 1, (37, 91)).astype(np.float32)
+    op = tl.reduce_mean if mean else tl.reduce_sum
+    r = op(tl.constant(x), dims, keep)
+    want = oracle.reduce(x, tuple(dims), keepdim=keep, mean=mean, f64=True)
+    assert r.shape == list(want.shape)
+    assert np.allclose(r.numpy(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_cache_and_clear():
+    x = tl.constant(np.ones((4, 4), np.float32))
+    y = tl.relu(x)
+    y.eval()
+    h0 = tl.stats()["cache_hits"]
+    z = tl.relu(x)
+    tl.evaluate([z])
+    tl.clear()
+    # node ids restart after clear(); the cache must not return the old result
+    x2 = tl.constant(-np.ones((4, 4), np.float32))
+    assert np.all(tl.relu(x2).numpy() == 0)
+    assert h0 >= 0
+
+
+def test_random_dag_matches_oracle():
+    """Small instance of the DCE / fusion stress graph: random ops over
+    [64, 64], 40% of the nodes unreachable, reductions at the sinks."""
+    tl.set_gemm_path("ffma")
+    rng = np.random.default_rng(4)
+    base = [rng.uniform(-0.5, 0.5, (64, 64)).astype(np.float32) for _ in range(4)]
+    lazy = [tl.constant(b) for b in base]
+    host = list(base)
+    reach = []
+    for i in range(60):
+        k = int(rng.integers(0, 5))
+        ia, ib = int(rng.integers(0, len(lazy))), int(rng.integers(0, len(lazy)))
+        if k == 0:
+            lazy.append(tl.relu(lazy[ia])); host.append(oracle.relu(host[ia]))
+        elif k == 1:
+            lazy.append(tl.sigmoid(lazy[ia])); host.append(oracle.sigmoid(host[ia]))
+        elif k == 2:
+            lazy.append(tl.add(lazy[ia], lazy[ib])); host.append(oracle.add(host[ia], host[ib]))
+        elif k == 3:
+            lazy.append(tl.multiply(lazy[ia], lazy[ib])); host.append(oracle.multiply(host[ia], host[ib]))
+        else:
+            lazy.append(tl.matmul(lazy[ia], lazy[ib])); host.append(oracle.matmul(host[ia], host[ib]))
+    sinks = list(range(len(lazy) - 6, len(lazy)))
+    outs = [tl.reduce_sum(lazy[s], [1]) for s in sinks]
+    tl.evaluate(outs)
+    for s, o in zip(sinks, outs):
+        want = oracle.reduce(host[s], (1,), f64=True)
+        scale = np.abs(host[s]).astype(np.float64).sum(axis=1) + 1e-30
+        assert np.all(np.abs(o.numpy() - want) <= 1e-4 * scale)

@@ -166,6 +166,14 @@ int decode_program(const ttc_chain_desc& d, bool acc_preloaded, DProgram* out) {
         };
         switch (in.op) {
             case TTC_OP_LOAD:
+                if (in.src == TTC_SRC_SLOT) {
+                    if (in.idx >= TTC_CHAIN_SLOTS || !slot_defined[in.idx])
+                        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d loads unset slot %d", pc,
+                                         in.idx);
+                    op = (uint8_t)(D_LOAD_S0 + in.idx);
+                    acc_defined = true;
+                    break;
+                }
                 if (in.idx >= d.n_inputs)
                     return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: step %d loads input %d of %d", pc, in.idx,
                                      d.n_inputs);

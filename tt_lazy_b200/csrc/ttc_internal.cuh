@@ -75,6 +75,10 @@ enum DOp : uint8_t {
     D_SAVE2,
     D_SAVE3,
     D_STORE,
+    D_LOAD_S0,
+    D_LOAD_S1,
+    D_LOAD_S2,
+    D_LOAD_S3,
     D_NUM_OPS
 };
 
@@ -261,6 +265,9 @@ __device__ __forceinline__ void run_program_io(const DProgram& P, float (&acc)[G
         break;                                                                                            \
     case D_SAVE0 + K:                                                                                     \
         if constexpr (NS > K) each<G, W>([&](int g, int w) { s[K % NS][g][w] = acc[g][w]; });             \
+        break;                                                                                            \
+    case D_LOAD_S0 + K:                                                                                   \
+        if constexpr (NS > K) each<G, W>([&](int g, int w) { acc[g][w] = s[K % NS][g][w]; });             \
         break;
                 TTC_SLOT_CASES(0)
                 TTC_SLOT_CASES(1)

@@ -1,0 +1,3 @@
+// EvaluationManager.hpp -- forwarding header: the declarations live in TapeExecutor.hpp / Tape.hpp.
+#pragma once
+#include "TapeExecutor.hpp"

@@ -1,0 +1,3 @@
+// MemoryManager.hpp -- forwarding header: the declarations live in TapeExecutor.hpp / Tape.hpp.
+#pragma once
+#include "TapeExecutor.hpp"
