@@ -639,6 +639,11 @@ void run_gemm_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan, 
     g.K = (int32_t)K;
     g.path = gemm_path();
     const std::vector<uint32_t> out_shape = {(uint32_t)M, (uint32_t)N};
+    auto fit_path = [&]() {
+        // "tf32" asks for the tensor-core path where it applies; shapes or
+        // layouts the tcgen05 kernel does not take run on the fp32 path.
+        if (g.path == TTC_GEMM_TF32 && ttc_gemm_select_path(&g) != TTC_GEMM_TF32) g.path = TTC_GEMM_FFMA;
+    };
     ProgramBuilder pb;
     Space sp;
     sp.rows = M;
@@ -666,6 +671,7 @@ void run_gemm_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan, 
         pb.d.outputs[pb.d.n_outputs++] = ttc_out_view{out.ptr(), N, 0};
         g.epilogue = pb.d;
     }
+    fit_path();
     check(ttc_gemm(&g));
     const NodeId node = plan.members.empty() ? op.node_id : plan.members[(size_t)stored[0]].node;
     set_output(ex, op, node, 0, out_shape, out);
