@@ -174,6 +174,27 @@ typedef struct {
 
 int ttc_eltwise_chain(const ttc_chain_desc* desc);
 
+/* Same computation as ttc_eltwise_chain, for callers that must not allocate
+ * device memory while they run: code inside a CUDA-graph capture, a serving
+ * or real-time loop that forbids allocation after start-up, or a host
+ * framework that owns every allocation itself. No counterpart in the
+ * reference (its backend runs on the CPU and allocates a Tensor per op).
+ *
+ * It calls no cudaMalloc, cudaFree or allocating library routine: the
+ * per-block partial sums of a reduction go to a fixed 1 MiB device array
+ * compiled into the library (every GPU that loads the library holds it until
+ * the process exits). A reduction that would need more partials than fit
+ * returns TTC_ERR_INVALID_ARGUMENT with the sizes in ttc_last_error(). The
+ * first call on a device looks up that array's device address (with the
+ * library's device current); make that first call before any stream capture.
+ * All calls share the one array and it keeps the last call's contents (the
+ * kernels overwrite every partial they read, nothing needs clearing), so
+ * calls that overlap on the GPU -- on different streams, or from different
+ * threads -- race: serialise them. It always uses the register-path kernels
+ * (the TMA-staged path is not taken), so results agree with
+ * ttc_eltwise_chain to rounding, not bit for bit, when a reduction is fused. */
+int ttc_eltwise_chain_noalloc(const ttc_chain_desc* desc);
+
 /* ------------------------------------------------------------ reductions
  * math::reduce_sum (src/backend/cpu/reduce_sum.cpp:9-62) and the MEAN type
  * of ReduceArgs (src/frontend/operations.hpp:13-14) over any set of dims of a

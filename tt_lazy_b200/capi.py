@@ -70,7 +70,7 @@ class MemoryStats(C.Structure):
 EXPORTS = ["ttc_last_error", "ttc_init", "ttc_shutdown", "ttc_device_count", "ttc_version", "ttc_get_stream",
            "ttc_set_stream", "ttc_synchronize", "ttc_malloc", "ttc_free", "ttc_memcpy_h2d", "ttc_memcpy_d2h",
            "ttc_memcpy_d2d", "ttc_memset_zero", "ttc_host_alloc", "ttc_host_free", "ttc_get_memory_stats",
-           "ttc_eltwise_chain", "ttc_reduce", "ttc_transpose", "ttc_copy2d", "ttc_gemm", "ttc_gemm_select_path",
+           "ttc_eltwise_chain", "ttc_eltwise_chain_noalloc", "ttc_reduce", "ttc_transpose", "ttc_copy2d", "ttc_gemm", "ttc_gemm_select_path",
            "ttc_comm_unique_id", "ttc_comm_init", "ttc_allreduce_sum", "ttc_comm_destroy"]
 
 
@@ -101,6 +101,7 @@ def lib():
         L.ttc_host_free.argtypes = [C.c_void_p]
         L.ttc_set_stream.argtypes = [C.c_void_p]
         L.ttc_eltwise_chain.argtypes = [C.POINTER(ChainDesc)]
+        L.ttc_eltwise_chain_noalloc.argtypes = [C.POINTER(ChainDesc)]
         L.ttc_gemm.argtypes = [C.POINTER(GemmDesc)]
         L.ttc_gemm_select_path.argtypes = [C.POINTER(GemmDesc)]
         L.ttc_reduce.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.c_int, C.POINTER(C.c_int32), C.c_int,

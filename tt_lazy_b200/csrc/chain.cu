@@ -240,8 +240,26 @@ bool vector_ok(const ttc_chain_desc& d) {
     return true;
 }
 
+// Caller-provided reduction scratch (the allocation-free entry point). When
+// null, partials live in the library's grow-only workspace.
+struct FixedScratch {
+    float* ptr;
+    size_t floats;
+};
+
+int scratch_for(size_t floats, const FixedScratch* fixed, void** out) {
+    if (!fixed) return workspace(floats * sizeof(float), out);
+    if (floats > fixed->floats)
+        return set_error(TTC_ERR_INVALID_ARGUMENT,
+                         "tt_cuda: ttc_eltwise_chain_noalloc: this reduction needs %zu bytes of scratch, the static "
+                         "buffer holds %zu bytes; use ttc_eltwise_chain",
+                         floats * sizeof(float), fixed->floats * sizeof(float));
+    *out = fixed->ptr;
+    return TTC_OK;
+}
+
 template <int W>
-int launch_chain(const ttc_chain_desc& d, ChainParams& p) {
+int launch_chain(const ttc_chain_desc& d, ChainParams& p, const FixedScratch* fixed) {
     cudaStream_t st = rt().stream;
     const int nseg = d.nseg;
     switch (d.reduce) {
@@ -258,7 +276,7 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p) {
             static int cap = occupancy_grid(chain_flat_kernel<W, true>);
             const int gx = (int)std::max<long long>(1, std::min<long long>(need, std::max(1, cap / nseg)));
             void* ws = nullptr;
-            if (int rc = workspace((size_t)gx * nseg * sizeof(float), &ws)) return rc;
+            if (int rc = scratch_for((size_t)gx * nseg, fixed, &ws)) return rc;
             p.partials = (float*)ws;
             chain_flat_kernel<W, true><<<dim3(gx, nseg), kThreads, 0, st>>>(p);
             finalize_all_kernel<<<nseg, 256, 0, st>>>(p.partials, gx, p.red_out, p.red_sseg, p.mean, p.count);
@@ -284,7 +302,7 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p) {
             p.nsplit = nsplit;
             if (nsplit > 1) {
                 void* ws = nullptr;
-                if (int rc = workspace((size_t)nsplit * nseg * p.cols * sizeof(float), &ws)) return rc;
+                if (int rc = scratch_for((size_t)nsplit * nseg * p.cols, fixed, &ws)) return rc;
                 p.partials = (float*)ws;
             }
             if (gx > 65535 * 64 || nsplit > 65535 || nseg > 65535)
@@ -318,7 +336,11 @@ void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg,
     count_launch();
 }
 
-int run_chain(const ttc_chain_desc& d) {
+static int run_chain_impl(const ttc_chain_desc& d, const FixedScratch* fixed);
+
+int run_chain(const ttc_chain_desc& d) { return run_chain_impl(d, nullptr); }
+
+static int run_chain_impl(const ttc_chain_desc& d, const FixedScratch* fixed) {
     if (d.rows < 0 || d.cols < 0 || d.nseg < 1)
         return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: chain shape rows=%d cols=%d nseg=%d is invalid", d.rows,
                          d.cols, d.nseg);
@@ -355,7 +377,7 @@ int run_chain(const ttc_chain_desc& d) {
         const char* e = getenv("TTC_CHAIN_TMA");
         return !(e && e[0] == '0');
     }();
-    if (tma_enabled) {
+    if (tma_enabled && !fixed) {
         bool launched = false;
         if (int rc = launch_chain_tma(d, p.prog, &launched)) return rc;
         if (launched) return TTC_OK;
@@ -369,7 +391,7 @@ int run_chain(const ttc_chain_desc& d) {
         return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: %llu vector chunks per segment exceed 2^31; split the tensor",
                          total);
     p.total = (unsigned)total;
-    return vec ? launch_chain<4>(d, p) : launch_chain<1>(d, p);
+    return vec ? launch_chain<4>(d, p, fixed) : launch_chain<1>(d, p, fixed);
 }
 
 }  // namespace ttc
@@ -493,3 +515,38 @@ int ttc_reduce(const float* in, const uint32_t* shape, int rank, const int32_t* 
 }
 
 }  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Allocation-free variant of ttc_eltwise_chain, for callers that cannot
+// allocate device memory while they run: code inside a CUDA-graph capture,
+// a real-time or serving loop that forbids allocation after start-up, or a
+// host framework that owns every allocation itself. The only scratch the
+// chain kernels need -- per-block partial sums of a reduction -- lives in a
+// file-scope device array of fixed size instead of the library workspace.
+namespace {
+constexpr size_t kNoAllocScratchFloats = 262144;  // 1 MiB; every GPU that loads the library holds it
+__device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+constexpr int kMaxDevices = 64;
+float* g_noalloc_scratch_dev[kMaxDevices] = {};  // device address of the array, per device
+}  // namespace
+
+extern "C" int ttc_eltwise_chain_noalloc(const ttc_chain_desc* desc) {
+    TTC_REQUIRE_INIT();
+    if (!desc) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: desc is NULL");
+    const int dev = rt().device;
+    if (dev < 0 || dev >= kMaxDevices) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: device %d", dev);
+    if (!g_noalloc_scratch_dev[dev]) {
+        // First call on this device: the host-side name of the array is not a
+        // device address, so look the address up once with the device current.
+        int cur = -1;
+        TTC_CUDA(cudaGetDevice(&cur));
+        if (cur != dev)
+            return set_error(TTC_ERR_INVALID_ARGUMENT,
+                             "tt_cuda: current device %d is not the library's device %d", cur, dev);
+        void* p = nullptr;
+        TTC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        g_noalloc_scratch_dev[dev] = static_cast<float*>(p);
+    }
+    const FixedScratch fixed{g_noalloc_scratch_dev[dev], kNoAllocScratchFloats};
+    return run_chain_impl(*desc, &fixed);
+}
