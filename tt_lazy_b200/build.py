@@ -35,9 +35,9 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 # is one IEEE op (bit-exact against the reference's separate passes); the GEMM
 # main loops use explicit fused multiply-adds where they want them.
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-fmad=false", "-Xcompiler", "-fPIC",
-                     "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC]
+                     "--expt-relaxed-constexpr", "-I" + INCLUDE, "-I" + CSRC, "-I" + OBJ]
 
-CUDA_SOURCES = ["runtime.cu", "chain.cu", "chain_tma.cu", "transpose.cu", "gemm_ffma.cu", "gemm_tc.cu"]
+CUDA_SOURCES = ["runtime.cu", "chain.cu", "chain_tma.cu", "chain_jit.cu", "transpose.cu", "gemm_ffma.cu", "gemm_tc.cu"]
 CPP_SOURCES = ["comm.cpp"]
 
 
@@ -71,9 +71,22 @@ def _headers(*dirs):
     return out
 
 
+def _embed_jit_source():
+    """chain_jit_device.cuh as a C++ raw string (the NVRTC source prefix)."""
+    src = os.path.join(CSRC, "chain_jit_device.cuh")
+    out = os.path.join(OBJ, "chain_jit_src.inc")
+    if _stale(out, [src]):
+        text = open(src).read()
+        assert ")TTJSRC" not in text
+        with open(out + ".tmp", "w") as f:
+            f.write('static const char kJitDeviceSrc[] = R"TTJSRC(' + text + ')TTJSRC";\n')
+        os.replace(out + ".tmp", out)
+    return out
+
+
 def build_cuda(verbose=False) -> str:
     os.makedirs(OBJ, exist_ok=True)
-    hdrs = _headers(CSRC, INCLUDE)
+    hdrs = _headers(CSRC, INCLUDE) + [_embed_jit_source()]
     nccl_inc, nccl_lib = _nccl_dirs()
     objs = []
     for src in CUDA_SOURCES:
@@ -98,7 +111,7 @@ def build_cuda(verbose=False) -> str:
     out = os.path.join(LIB, "libtt_cuda.so")
     if _stale(out, objs):
         cmd = [NVCC] + ARCH + ["-shared", "-cudart", "static", "-o", out + ".tmp"] + objs + [
-            "-Xlinker", "-soname,libtt_cuda.so"]
+            "-Xlinker", "-soname,libtt_cuda.so", "-ldl"]
         if nccl_lib:
             cmd += ["-L" + nccl_lib, "-l:libnccl.so.2", "-Xlinker", "-rpath," + nccl_lib]
         _run(cmd, verbose)

@@ -20,6 +20,8 @@ namespace ttc {
 
 // Staged (TMA-fed) variant, chain_tma.cu: launches when the layout allows it.
 int launch_chain_tma(const ttc_chain_desc& d, const DProgram& prog, bool* launched);
+// Program-specialised variant, chain_jit.cu: launches when compiled.
+int launch_chain_jit(const ttc_chain_desc& d, const DProgram& prog, bool* launched);
 
 namespace {
 
@@ -377,6 +379,15 @@ static int run_chain_impl(const ttc_chain_desc& d, const FixedScratch* fixed) {
         const char* e = getenv("TTC_CHAIN_TMA");
         return !(e && e[0] == '0');
     }();
+    static const bool jit_enabled = [] {
+        const char* e = getenv("TTC_CHAIN_JIT");
+        return !(e && e[0] == '0');
+    }();
+    if (jit_enabled && !fixed) {
+        bool launched = false;
+        if (int rc = launch_chain_jit(d, p.prog, &launched)) return rc;
+        if (launched) return TTC_OK;
+    }
     if (tma_enabled && !fixed) {
         bool launched = false;
         if (int rc = launch_chain_tma(d, p.prog, &launched)) return rc;

@@ -1,0 +1,251 @@
+// chain_jit_device.cuh -- kernel templates of the specialised element-wise
+// chain. At run time chain_jit.cu turns one fused program into a small Body
+// struct of straight-line code (every operand index, input kind and program
+// step fixed), appends it to this file's text and compiles the result once
+// for sm_100a with NVRTC; the kernel is cached per distinct program. The
+// structures (grid-stride over 128-bit column quads, warp per row for row
+// sums, column blocks with row splits for column sums) are the same as the
+// interpreted kernels of chain.cu, so results and partial-sum layouts match.
+//
+// The file is valid under nvcc (the host side uses the parameter struct) and
+// under NVRTC (no standard headers). Everything runs with -fmad=false: each
+// program step is one IEEE op.
+#pragma once
+
+#define TTJ_MAX_IN 6
+#define TTJ_MAX_OUT 4
+
+struct JInView {
+    const float* ptr;
+    long long sr, sc, sseg;
+};
+struct JOutView {
+    float* ptr;
+    long long sr, sseg;
+};
+struct JFastDiv {
+    unsigned d, m, s;
+};
+
+struct JParams {
+    JInView in[TTJ_MAX_IN];
+    JOutView out[TTJ_MAX_OUT];
+    int rows, cols, nseg;
+    unsigned cpr;
+    JFastDiv cpr_div;
+    unsigned total;
+    float* red_out;
+    long long red_sseg;
+    float* partials;
+    int nsplit, rows_per_split;
+    int mean;
+    double count;
+};
+
+#if defined(__CUDACC_RTC__) || defined(__CUDA_ARCH__)
+
+#define TTJ_THREADS 256
+
+__device__ __forceinline__ unsigned ttj_fdiv(unsigned n, const JFastDiv& f) { return (__umulhi(n, f.m) + n) >> f.s; }
+
+__device__ __forceinline__ float ttj_relu(float x) { return (0.0f < x) ? x : 0.0f; }
+
+// e^x rounded once from a double approximation with relative error below
+// 2^-44 (table-driven reduction, P. T. P. Tang, ACM TOMS 15(2), 1989: x =
+// (64 m + j) ln2/64 + r, |r| <= ln2/128, e^r by its degree-4 Taylor
+// polynomial), i.e. the correctly rounded float except within 2^-44 of a
+// rounding midpoint -- the same values as glibc's expf on all but ~0.07% of
+// inputs, where glibc is the one off by an ulp.
+__shared__ double ttj_exp2_tab[64];
+
+__device__ __forceinline__ void ttj_exp_table_init() {
+    for (int i = threadIdx.x; i < 64; i += blockDim.x) ttj_exp2_tab[i] = exp2((double)i * (1.0 / 64.0));
+}
+
+__device__ __forceinline__ float ttj_exp(float x) {
+    if (x != x) return x;
+    if (x > 89.0f) return __int_as_float(0x7f800000);
+    if (x < -104.0f) return 0.0f;
+    const int k = __float2int_rn(x * 92.33248261689366f);
+    const double r = fma(-(double)k, 0.010830424696249145, (double)x);
+    double p = fma(r, 1.0 / 24.0, 1.0 / 6.0);
+    p = fma(p, r, 0.5);
+    p = fma(p, r, 1.0);
+    p = fma(p, r, 1.0);
+    double e = p * ttj_exp2_tab[k & 63];
+    e = __longlong_as_double(__double_as_longlong(e) + (long long)(k >> 6) * (1ll << 52));
+    return __double2float_rn(e);
+}
+
+__device__ __forceinline__ float ttj_sigmoid(float x) { return 1.0f / (1.0f + ttj_exp(-x)); }
+
+// Operand kinds: 0 full (contiguous columns), 1 row broadcast ([1,C]),
+// 2 column broadcast ([R,1]).
+template <int W, int KIND>
+__device__ __forceinline__ void ttj_load(const JInView& v, long long seg, long long row, long long col, float* d) {
+    if (KIND == 2) {
+        const float s = __ldg(v.ptr + seg * v.sseg + row * v.sr);
+#pragma unroll
+        for (int w = 0; w < W; ++w) d[w] = s;
+    } else {
+        const float* q = v.ptr + seg * v.sseg + (KIND == 1 ? 0 : row * v.sr) + col;
+        if (W == 4) {
+            const float4 t = __ldg(reinterpret_cast<const float4*>(q));
+            d[0] = t.x;
+            d[1] = t.y;
+            d[2] = t.z;
+            d[3] = t.w;
+        } else {
+            d[0] = __ldg(q);
+        }
+    }
+}
+
+template <int W>
+__device__ __forceinline__ void ttj_store(const JOutView& v, long long seg, long long row, long long col,
+                                          const float* s) {
+    float* q = v.ptr + seg * v.sseg + row * v.sr + col;
+    if (W == 4)
+        *reinterpret_cast<float4*>(q) = make_float4(s[0], s[1], s[2], s[3]);
+    else
+        q[0] = s[0];
+}
+
+__device__ __forceinline__ float ttj_warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------- kernels
+template <int W, int G, bool SIG, bool REDUCE_ALL, class Body>
+__device__ __forceinline__ void ttj_flat(const JParams& p) {
+    if (SIG) {
+        ttj_exp_table_init();
+        __syncthreads();
+    }
+    const long long seg = blockIdx.y;
+    float sum = 0.0f;
+    for (unsigned blk = blockIdx.x; (unsigned long long)blk * (TTJ_THREADS * G) < p.total; blk += gridDim.x) {
+        const unsigned q0 = blk * (TTJ_THREADS * G) + threadIdx.x;
+        long long row[G], col[G];
+        bool valid[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const unsigned q = q0 + g * TTJ_THREADS;
+            valid[g] = q < p.total;
+            const unsigned r = ttj_fdiv(q, p.cpr_div);
+            row[g] = r;
+            col[g] = (long long)(q - r * p.cpr) * W;
+        }
+        float acc[G][W];
+        Body::run(p, acc, seg, row, col, valid);
+        if (REDUCE_ALL) {
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                if (valid[g])
+#pragma unroll
+                    for (int w = 0; w < W; ++w) sum += acc[g][w];
+        }
+    }
+    if (REDUCE_ALL) {
+        __shared__ float red[TTJ_THREADS / 32];
+        sum = ttj_warp_sum(sum);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+            float v = threadIdx.x < TTJ_THREADS / 32 ? red[threadIdx.x] : 0.0f;
+            v = ttj_warp_sum(v);
+            if (threadIdx.x == 0) p.partials[seg * gridDim.x + blockIdx.x] = v;
+        }
+    }
+}
+
+template <int W, int G, bool SIG, class Body>
+__device__ __forceinline__ void ttj_rows(const JParams& p) {
+    if (SIG) {
+        ttj_exp_table_init();
+        __syncthreads();
+    }
+    const long long seg = blockIdx.y;
+    const int lane = threadIdx.x & 31;
+    const unsigned warp = (blockIdx.x * TTJ_THREADS + threadIdx.x) >> 5;
+    const unsigned nwarps = (gridDim.x * TTJ_THREADS) >> 5;
+    for (unsigned r = warp; r < (unsigned)p.rows; r += nwarps) {
+        float sum = 0.0f;
+        for (unsigned c0 = lane; c0 < p.cpr; c0 += 32 * G) {
+            long long row[G], col[G];
+            bool valid[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const unsigned ch = c0 + g * 32;
+                valid[g] = ch < p.cpr;
+                row[g] = r;
+                col[g] = (long long)ch * W;
+            }
+            float acc[G][W];
+            Body::run(p, acc, seg, row, col, valid);
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                if (valid[g])
+#pragma unroll
+                    for (int w = 0; w < W; ++w) sum += acc[g][w];
+        }
+        sum = ttj_warp_sum(sum);
+        if (lane == 0) p.red_out[seg * p.red_sseg + r] = p.mean ? (float)((double)sum / p.count) : sum;
+    }
+}
+
+template <int W, int G, bool SIG, class Body>
+__device__ __forceinline__ void ttj_cols(const JParams& p) {
+    const int NW = TTJ_THREADS / 32;
+    if (SIG) {
+        ttj_exp_table_init();
+        __syncthreads();
+    }
+    const long long seg = blockIdx.z;
+    const int split = blockIdx.y;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const unsigned ch = blockIdx.x * 32 + lane;
+    const bool col_ok = ch < p.cpr;
+    const int r0 = split * p.rows_per_split;
+    const int r1 = min(p.rows, r0 + p.rows_per_split);
+    float s[W];
+#pragma unroll
+    for (int w = 0; w < W; ++w) s[w] = 0.0f;
+    for (int r = r0 + warp; r < r1; r += NW * G) {
+        long long row[G], col[G];
+        bool valid[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            row[g] = r + g * NW;
+            col[g] = (long long)ch * W;
+            valid[g] = col_ok && row[g] < r1;
+        }
+        float acc[G][W];
+        Body::run(p, acc, seg, row, col, valid);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            if (valid[g])
+#pragma unroll
+                for (int w = 0; w < W; ++w) s[w] += acc[g][w];
+    }
+    __shared__ float sm[TTJ_THREADS / 32][32 * W + 1];
+#pragma unroll
+    for (int w = 0; w < W; ++w) sm[warp][lane * W + w] = s[w];
+    __syncthreads();
+    for (int i = threadIdx.x; i < 32 * W; i += TTJ_THREADS) {
+        float t = 0.0f;
+#pragma unroll
+        for (int k = 0; k < NW; ++k) t += sm[k][i];
+        const long long c = (long long)blockIdx.x * 32 * W + i;
+        if (c < p.cols) {
+            if (p.nsplit == 1)
+                p.red_out[seg * p.red_sseg + c] = p.mean ? (float)((double)t / p.count) : t;
+            else
+                p.partials[((long long)seg * p.nsplit + split) * p.cols + c] = t;
+        }
+    }
+}
+
+#endif  // device compilation
