@@ -97,8 +97,21 @@ def test_bandwidth_graph_views_and_chains():
         y = tl.multiply(tl.sigmoid(ch), tl.relu(tl.add(ch, ch)))
         outs.append(tl.reduce_sum(y, [1]))
     t = ops(outs)
-    assert t[:2] == ["Transpose", "Split"]
-    assert t[2:] == ["FusedChain[sigmoid -> add -> relu -> multiply -> reduce]"] * 8
+    assert t == ["Transpose", "Split", "FusedChain[sigmoid -> add -> relu -> multiply -> reduce x8 segments]"]
+
+
+def test_segment_fusion_needs_consecutive_equal_chunks():
+    A = c((64, 48))
+    chunks = tl.split(A, 20, 0)  # 20, 20, 20, 4: the ragged last chunk runs alone
+    outs = [tl.reduce_sum(tl.relu(ch), [1]) for ch in chunks]
+    t = ops(outs)
+    assert t == ["Split", "FusedChain[relu -> reduce x3 segments]", "FusedChain[relu -> reduce]"]
+    # different programs per chunk do not merge
+    B = c((64, 48), 1)
+    ch = tl.split(B, 16, 0)
+    outs = [tl.relu(ch[0]), tl.sigmoid(ch[1]), tl.relu(ch[2]), tl.relu(ch[3])]
+    t = ops(outs)
+    assert t.count("FusedChain[relu x2 segments]") == 1 and "FusedChain[sigmoid]" in t
 
 
 def test_dead_code_is_not_on_the_tape():

@@ -148,6 +148,43 @@ def test_transpose_split_views_feed_fused_chains():
         assert np.array_equal(p.numpy(), want)
 
 
+@pytest.mark.parametrize("transposed", [False, True])
+def test_segmented_chains_match_per_chunk_oracle(transposed):
+    # one segmented launch for the equal chunks; stored intermediates and the
+    # per-chunk reductions of every segment are returned separately
+    rng = np.random.default_rng(5)
+    a = rng.uniform(-2, 2, (192, 160)).astype(np.float32)
+    src = tl.transpose(tl.constant(a)) if transposed else tl.constant(a)
+    base = oracle.transpose(a) if transposed else a
+    chunks = tl.split(src, 48, 1)  # 160 or 192 columns: ragged last chunk when 160
+    mids, reds = [], []
+    for ch in chunks:
+        m = tl.relu(tl.add(tl.sigmoid(ch), ch))
+        mids.append(m)
+        reds.append(tl.reduce_mean(tl.multiply(m, ch), [0]))
+    tl.evaluate(mids + reds)
+    for i, (m, r) in enumerate(zip(mids, reds)):
+        ch = np.ascontiguousarray(base[:, 48 * i:48 * (i + 1)])
+        mo = oracle.relu(oracle.add(oracle.sigmoid(ch), ch))
+        assert m.shape == list(ch.shape)
+        assert np.array_equal(m.numpy(), mo)
+        want = oracle.reduce(oracle.multiply(mo, ch), (0,), mean=True, f64=True)
+        assert np.allclose(r.numpy(), want, rtol=1e-5, atol=1e-6)
+
+
+def test_segmented_chain_on_strided_rank3_chunks_falls_back():
+    # chunks of a middle-dim split are not addressable by (row, col) strides:
+    # the segments then run one by one, with the same results
+    rng = np.random.default_rng(6)
+    a = rng.uniform(-1, 1, (4, 12, 8)).astype(np.float32)
+    chunks = tl.split(tl.constant(a), 3, 1)
+    outs = [tl.multiply(tl.relu(ch), ch) for ch in chunks]
+    tl.evaluate(outs)
+    for o, ch in zip(outs, oracle.split(a, 3, 1)):
+        ch = np.ascontiguousarray(ch)
+        assert np.array_equal(o.numpy(), oracle.multiply(oracle.relu(ch), ch))
+
+
 @pytest.mark.parametrize("dims,keep", [([], False), ([0], False), ([1], True), ([0, 1], False), ([-1], False)])
 @pytest.mark.parametrize("mean", [False, True])
 def test_reduce_semantics(dims, keep, mean):

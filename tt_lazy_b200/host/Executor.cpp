@@ -259,9 +259,11 @@ int64_t numel(const std::vector<uint32_t>& s) {
     return n;
 }
 
-DeviceView new_buffer(const std::vector<uint32_t>& shape) {
+// A dense row-major buffer for `copies` tensors of `shape` (the view covers
+// the first; copy s starts at element s * numel(shape)).
+DeviceView new_buffer(const std::vector<uint32_t>& shape, int copies = 1) {
     DeviceView v;
-    v.buf = MemoryManager::instance().allocate((size_t)std::max<int64_t>(numel(shape), 1) * sizeof(float));
+    v.buf = MemoryManager::instance().allocate((size_t)std::max<int64_t>(numel(shape) * copies, 1) * sizeof(float));
     int64_t s = 1;
     for (int i = (int)shape.size() - 1; i >= 0; --i) {
         v.strides[i] = s;
@@ -480,8 +482,18 @@ bool operand_view(const Operand& o, const std::vector<uint32_t>& out, const Spac
     return false;
 }
 
-// Runs a fused chain plan (members [0, nmembers)).
-void run_chain_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan, std::vector<Operand> ext) {
+// Thrown when a segmented chain cannot address its segments with one stride
+// per operand; the caller then runs the segments one by one.
+struct SegmentLayoutError : std::runtime_error {
+    using std::runtime_error::runtime_error;
+};
+
+// Runs a fused chain plan. A segmented plan (nseg > 1) runs all segments in
+// one launch: `ext` holds segment 0's operands and seg_strides[k] the element
+// distance between consecutive segments of operand k (0 when shared).
+void run_chain_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan, std::vector<Operand> ext,
+                    const std::vector<int64_t>* seg_strides = nullptr) {
+    const int nseg = seg_strides ? plan.nseg : 1;
     const auto& members = plan.members;
     const bool has_reduce = members.back().op == FusionPlan::REDUCE;
     const size_t n_elt = has_reduce ? members.size() - 1 : members.size();
@@ -507,30 +519,33 @@ void run_chain_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan,
     }
     ProgramBuilder pb;
     auto& d = pb.d;
-    d.nseg = 1;
+    d.nseg = nseg;
     d.rows = (int32_t)(sp.transposed ? sp.cols : sp.rows);
     d.cols = (int32_t)(sp.transposed ? sp.rows : sp.cols);
     // inputs
     for (size_t k = 0; k < ext.size(); ++k) {
         ttc_in_view v;
+        const int64_t ss = nseg > 1 ? (*seg_strides)[k] : 0;
         if (!operand_view(ext[k], space_shape, sp, &v)) {
+            if (ss != 0) throw SegmentLayoutError("segment operand needs a dense copy");
             ext[k] = contiguous(ext[k]);
             if (!operand_view(ext[k], space_shape, sp, &v))
                 throw std::runtime_error("Broadcasting addition not implemented for these shapes");
         }
+        v.seg_stride = ss;
         pb.input_of_ext[(int)k] = d.n_inputs;
         d.inputs[d.n_inputs++] = v;
     }
     const auto stored = build_program(pb, plan, members.size(), INT32_MIN);
-    // outputs of escaping element-wise members
+    // outputs of escaping element-wise members (all segments in one buffer)
     std::vector<DeviceView> outs;
     for (int m : stored) {
-        DeviceView v = new_buffer(members[(size_t)m].shape);
+        DeviceView v = new_buffer(members[(size_t)m].shape, nseg);
         if (sp.transposed) {  // allocate physical [C, R]; expose as a transposed view
             v.strides[0] = 1;
             v.strides[1] = sp.rows;
         }
-        d.outputs[d.n_outputs++] = ttc_out_view{v.ptr(), d.cols, 0};
+        d.outputs[d.n_outputs++] = ttc_out_view{v.ptr(), d.cols, numel(members[(size_t)m].shape)};
         outs.push_back(v);
     }
     DeviceView red_out;
@@ -579,15 +594,26 @@ void run_chain_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan,
         }
         d.reduce = mode;
         d.reduce_mean = r.mean ? 1 : 0;
-        red_out = new_buffer(r.shape);
+        red_out = new_buffer(r.shape, nseg);
         d.reduce_out = red_out.ptr();
+        d.reduce_seg_stride = numel(r.shape);
     }
     check(ttc_eltwise_chain(&d));
-    for (size_t j = 0; j < stored.size(); ++j) {
-        const auto& m = members[(size_t)stored[j]];
-        set_output(ex, op, m.node, 0, m.shape, outs[j]);
+    // segment s of every result sits s * numel(shape) elements into its buffer
+    auto seg_view = [](DeviceView v, const std::vector<uint32_t>& shape, int s) {
+        v.offset += (int64_t)s * numel(shape);
+        return v;
+    };
+    auto node_of = [&](size_t m, int s) { return nseg > 1 ? plan.seg_nodes[(size_t)s][m] : members[m].node; };
+    for (int s = 0; s < nseg; ++s) {
+        for (size_t j = 0; j < stored.size(); ++j) {
+            const auto& m = members[(size_t)stored[j]];
+            set_output(ex, op, node_of((size_t)stored[j], s), 0, m.shape, seg_view(outs[j], m.shape, s));
+        }
+        if (has_reduce)
+            set_output(ex, op, node_of(members.size() - 1, s), 0, members.back().shape,
+                       seg_view(red_out, members.back().shape, s));
     }
-    if (has_reduce) set_output(ex, op, members.back().node, 0, members.back().shape, red_out);
 }
 
 // matmul operand -> (ptr, ld, transposed) for ttc_gemm, folding a transposed view.
@@ -792,14 +818,65 @@ void handle_fused_mlp(TapeOperation& op, TapeExecutor& ex) {
     run_gemm_plan(op, ex, plan, ext);
 }
 
+// Segment s of a segmented plan as a plain chain plan.
+FusionPlan segment_plan(const FusionPlan& p, int s) {
+    FusionPlan q = p;
+    q.nseg = 1;
+    q.seg_nodes.clear();
+    q.ext_seg_index.clear();
+    for (size_t m = 0; m < q.members.size(); ++m) q.members[m].node = p.seg_nodes[(size_t)s][m];
+    for (size_t k = 0; k < q.externals.size(); ++k)
+        if (p.ext_seg_index[k] >= 0) q.externals[k].index = (uint16_t)(p.ext_seg_index[k] + s);
+    return q;
+}
+
+void run_chain_unsegmented(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan);
+
 void handle_fused_chain(TapeOperation& op, TapeExecutor& ex) {
+    const FusionPlan& plan = *op.plan;
+    if (plan.nseg <= 1) {
+        run_chain_unsegmented(op, ex, plan);
+        return;
+    }
+    // Segment k of a split operand must sit a fixed stride after segment k-1
+    // in the same buffer with the same strides (equal chunks of one split).
     std::vector<Operand> ext;
-    for (const auto& o : op.plan->externals) ext.push_back(resolve(o, ex, "fused chain"));
+    std::vector<int64_t> seg_strides;
+    bool uniform = true;
+    for (size_t k = 0; k < plan.externals.size(); ++k) {
+        ext.push_back(resolve(plan.externals[k], ex, "fused chain"));
+        int64_t stride = 0;
+        if (plan.ext_seg_index[k] >= 0) {
+            for (int s = 1; s < plan.nseg && uniform; ++s) {
+                OperandRef r = plan.externals[k];
+                r.index = (uint16_t)(plan.ext_seg_index[k] + s);
+                const Operand o = resolve(r, ex, "fused chain");
+                const int64_t dist = o.view.offset - ext[k].view.offset;
+                if (s == 1) stride = dist;
+                uniform = o.view.buf == ext[k].view.buf && o.shape == ext[k].shape && dist == s * stride &&
+                          std::equal(o.view.strides, o.view.strides + 4, ext[k].view.strides) && stride != 0;
+            }
+        }
+        seg_strides.push_back(stride);
+    }
+    if (uniform) {
+        try {
+            run_chain_plan(op, ex, plan, ext, &seg_strides);
+            return;
+        } catch (const SegmentLayoutError&) {
+        } catch (const std::length_error&) {
+        }
+    }
+    for (int s = 0; s < plan.nseg; ++s) run_chain_unsegmented(op, ex, segment_plan(plan, s));
+}
+
+void run_chain_unsegmented(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan) {
+    std::vector<Operand> ext;
+    for (const auto& o : plan.externals) ext.push_back(resolve(o, ex, "fused chain"));
     try {
-        run_chain_plan(op, ex, *op.plan, ext);
+        run_chain_plan(op, ex, plan, ext);
     } catch (const std::length_error&) {
         // Program over the register budget: run the members one by one.
-        const auto& plan = *op.plan;
         std::vector<Operand> vals(plan.members.size());
         for (size_t m = 0; m < plan.members.size(); ++m) {
             FusionPlan one;

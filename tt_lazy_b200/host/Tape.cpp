@@ -34,6 +34,8 @@ void Tape::build_node_map() {
         for (NodeId n : op->output_nodes) node_to_op_[n] = op.get();
         if (op->plan) {
             for (const auto& m : op->plan->members) node_to_op_[m.node] = op.get();
+            for (const auto& seg : op->plan->seg_nodes)
+                for (NodeId s : seg) node_to_op_[s] = op.get();
             if (op->plan->has_matmul) node_to_op_[op->plan->matmul_node] = op.get();
         }
     }
@@ -88,6 +90,7 @@ std::string FusionPlan::describe() const {
     std::ostringstream o;
     if (has_matmul) o << "matmul" << (members.empty() ? "" : " -> ");
     for (size_t i = 0; i < members.size(); ++i) o << (i ? " -> " : "") << names[members[i].op];
+    if (nseg > 1) o << " x" << nseg << " segments";
     return o.str();
 }
 
@@ -108,6 +111,7 @@ void TapeGenerator::register_default_passes() {
     register_optimization_pass(std::make_unique<DeadCodeEliminationPass>());
     register_optimization_pass(std::make_unique<MLPFusionPass>());
     register_optimization_pass(std::make_unique<EltwiseFusionPass>());
+    register_optimization_pass(std::make_unique<SegmentFusionPass>());
     default_passes_registered_ = true;
 }
 
@@ -326,6 +330,8 @@ bool rebuild(std::vector<std::unique_ptr<TapeOperation>>& ops, std::vector<std::
         for (NodeId o : op.output_nodes) unit_of_node[o] = (int)u;
         if (op.plan) {
             for (auto& m : op.plan->members) unit_of_node[m.node] = (int)u;
+            for (const auto& seg : op.plan->seg_nodes)
+                for (NodeId s : seg) unit_of_node[s] = (int)u;
             if (op.plan->has_matmul) unit_of_node[op.plan->matmul_node] = (int)u;
         }
     }
@@ -727,4 +733,112 @@ int EltwiseFusionPass::apply(Tape& tape, const std::vector<Tensor>& outputs) {
     if (!rebuild(ops, fused, group_of)) return 0;  // would be cyclic: keep the unfused tape
     rebuild_node_map(tape);
     return fused_count;
+}
+
+// ------------------------------------------------------------- segment fusion
+int SegmentFusionPass::apply(Tape& tape, const std::vector<Tensor>& outputs) {
+    (void)outputs;
+    auto& ops = get_operations(tape);
+    const size_t n = ops.size();
+    auto is_split = [](NodeId id) {
+        const Node* nd = Context::instance().get_node(id);
+        return nd && nd->is<SplitArgs>();
+    };
+    // (signature, split node) -> [(chunk index, tape position)]
+    std::map<std::pair<std::string, NodeId>, std::vector<std::pair<int, size_t>>> groups;
+    for (size_t i = 0; i < n; ++i) {
+        const TapeOperation& op = *ops[i];
+        if (!op.plan || op.plan->has_matmul || op.plan->nseg != 1 || op.op_type != FusedChainArgs::type_id())
+            continue;
+        const FusionPlan& P = *op.plan;
+        std::ostringstream sig;
+        for (const auto& m : P.members) {
+            sig << m.op << "(";
+            for (int a : m.args) sig << a << ",";
+            sig << ")" << m.escapes << m.keepdim << m.mean << "[";
+            for (auto d : m.shape) sig << d << ",";
+            sig << "]{";
+            for (auto d : m.dims) sig << d << ",";
+            sig << "};";
+        }
+        NodeId split = 0;
+        int chunk = -1;
+        bool ok = true;
+        for (const auto& e : P.externals) {
+            if (e.lazy && is_split(e.node)) {
+                if (split == 0) {
+                    split = e.node;
+                    chunk = e.index;
+                } else if (e.node != split || e.index != chunk) {
+                    ok = false;  // every varying operand must read the same chunk
+                    break;
+                }
+                // the chunk's own shape (a ragged last chunk differs)
+                const auto& shapes = Context::instance().get_node(e.node)->output_shapes();
+                sig << "S[";
+                if (e.index < shapes.size())
+                    for (auto d : shapes[e.index]) sig << d << ",";
+                sig << "];";
+            } else if (e.lazy) {
+                sig << "L" << e.node << ":" << e.index << ";";
+            } else {
+                const void* id = e.tensor.host_data();
+                if (!id && e.tensor.has_device()) id = e.tensor.device().ptr();
+                if (!id) {
+                    ok = false;
+                    break;
+                }
+                sig << "C" << id << ":" << e.tensor.total_elements() << ";";
+            }
+        }
+        if (!ok || split == 0) continue;
+        groups[{sig.str(), split}].push_back({chunk, i});
+    }
+    std::vector<int> group_of(n, -1);
+    std::vector<std::unique_ptr<TapeOperation>> fused;
+    for (auto& [key, v] : groups) {
+        std::sort(v.begin(), v.end());
+        size_t a = 0;
+        while (a < v.size()) {
+            size_t b = a + 1;
+            while (b < v.size() && v[b].first == v[b - 1].first + 1) ++b;
+            if (b - a >= 2) {
+                const TapeOperation& first = *ops[v[a].second];
+                auto plan = std::make_shared<FusionPlan>(*first.plan);
+                plan->nseg = (int)(b - a);
+                plan->ext_seg_index.clear();
+                for (const auto& e : plan->externals)
+                    plan->ext_seg_index.push_back(e.lazy && e.node == key.second ? (int)e.index : -1);
+                auto op = std::make_unique<TapeOperation>(ops[v[b - 1].second]->node_id, FusedChainArgs::type_id());
+                for (size_t s = a; s < b; ++s) {
+                    const TapeOperation& seg = *ops[v[s].second];
+                    std::vector<NodeId> nodes;
+                    for (const auto& m : seg.plan->members) nodes.push_back(m.node);
+                    plan->seg_nodes.push_back(nodes);
+                    for (NodeId o : seg.output_nodes) op->output_nodes.push_back(o);
+                    group_of[v[s].second] = (int)fused.size();
+                }
+                op->output_shapes = first.output_shapes;
+                op->input_nodes = first.input_nodes;
+                op->constant_inputs = first.constant_inputs;
+                // operands: every segment's chunk (keeps them alive until this op ran)
+                op->operands = plan->externals;
+                for (int s = 1; s < plan->nseg; ++s)
+                    for (size_t k = 0; k < plan->externals.size(); ++k)
+                        if (plan->ext_seg_index[k] >= 0) {
+                            OperandRef r = plan->externals[k];
+                            r.index = (uint16_t)(plan->ext_seg_index[k] + s);
+                            op->operands.push_back(r);
+                        }
+                op->plan = plan;
+                fused.push_back(std::move(op));
+            }
+            a = b;
+        }
+    }
+    if (fused.empty()) return 0;
+    const int count = (int)fused.size();
+    if (!rebuild(ops, fused, group_of)) return 0;
+    rebuild_node_map(tape);
+    return count;
 }

@@ -61,6 +61,13 @@ struct FusionPlan {
     bool matmul_escapes = false;
     std::vector<Member> members;
     std::vector<OperandRef> externals;
+    // Segmented chain (SegmentFusionPass): the same chain over `nseg`
+    // consecutive chunks of one split. External k reads split output
+    // ext_seg_index[k] + s in segment s (or is shared when -1); member m of
+    // segment s is graph node seg_nodes[s][m].
+    int nseg = 1;
+    std::vector<int> ext_seg_index;
+    std::vector<std::vector<NodeId>> seg_nodes;
     std::string describe() const;
 };
 
@@ -187,6 +194,17 @@ class EltwiseFusionPass : public TapeOptimizationPass {
     std::string name() const override { return "EltwiseFusion"; }
     static constexpr int ELTWISE_FUSION_PRIORITY = 60;
     int priority() const override { return ELTWISE_FUSION_PRIORITY; }
+};
+
+// Merges fused chains that run the same program on consecutive chunks of
+// one split (e.g. a per-chunk chain after transpose -> split) into one
+// segmented chain: one kernel launch over all chunks instead of one each.
+class SegmentFusionPass : public TapeOptimizationPass {
+   public:
+    int apply(Tape& tape, const std::vector<Tensor>& outputs) override;
+    std::string name() const override { return "SegmentFusion"; }
+    static constexpr int SEGMENT_FUSION_PRIORITY = 70;
+    int priority() const override { return SEGMENT_FUSION_PRIORITY; }
 };
 
 // Internal op types of fused tape operations.
