@@ -82,6 +82,21 @@ def test_sigmoid_ulp(ttc, golden):
     assert ulp_dist(got.ravel(), golden["sig_y"]).max() <= 3
 
 
+def test_sigmoid_dense_sweep_matches_correctly_rounded_formula(ttc):
+    """Every 64th float of [-104, 104] (both signs, ~35M inputs): sigmoid's exp
+    is correctly rounded except within ~2^-48 of a rounding midpoint, so the
+    kernel equals 1/(1+e^-x) with a correctly rounded exp on all but a
+    handful of inputs, and is never more than 1 ulp away."""
+    top = np.float32(104.0).view(np.int32)
+    bits = np.arange(0, top, 64, dtype=np.int32)
+    x = np.concatenate([bits.view(np.float32), (-bits.view(np.float32))])
+    x = np.concatenate([x, np.zeros((-x.size) % 4096, np.float32)]).reshape(-1, 4096)
+    got = run_unary(ttc, ttc.OP_SIGMOID, x)
+    d = ulp_dist(got, oracle.sigmoid_cr(x))
+    assert d.max() <= 1
+    assert np.count_nonzero(d) <= 16, np.count_nonzero(d)
+
+
 @pytest.mark.parametrize("shape", SHAPES)
 @pytest.mark.parametrize("op", ["add", "mul"])
 def test_binary_bit_exact(ttc, shape, op):

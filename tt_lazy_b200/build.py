@@ -9,7 +9,7 @@ Produces, under ``tt_lazy_b200/lib/``:
   passes / handlers) linked against ``libtt_cuda.so``.
 * ``_tt_lazy*.so``   -- the pybind11 module over the front end (tests, bench).
 
-Run ``python -m tt_lazy_b200.build`` (or ``__graft_entry__.build()``).
+Run ``python tt_lazy_b200/build.py`` (or ``__graft_entry__.build()``).
 Objects are rebuilt only when a source or header is newer than the output.
 """
 from __future__ import annotations
@@ -72,11 +72,13 @@ def _headers(*dirs):
 
 
 def _embed_jit_source():
-    """chain_jit_device.cuh as a C++ raw string (the NVRTC source prefix)."""
-    src = os.path.join(CSRC, "chain_jit_device.cuh")
+    """exp_cr.cuh + chain_jit_device.cuh as a C++ raw string (the NVRTC
+    source prefix; NVRTC gets no include path)."""
+    srcs = [os.path.join(CSRC, "exp_cr.cuh"), os.path.join(CSRC, "chain_jit_device.cuh")]
     out = os.path.join(OBJ, "chain_jit_src.inc")
-    if _stale(out, [src]):
-        text = open(src).read()
+    if _stale(out, srcs):
+        text = "\n".join(line for s in srcs for line in open(s).read().splitlines()
+                         if line.strip() != "#pragma once") + "\n"
         assert ")TTJSRC" not in text
         with open(out + ".tmp", "w") as f:
             f.write('static const char kJitDeviceSrc[] = R"TTJSRC(' + text + ')TTJSRC";\n')

@@ -44,40 +44,23 @@ struct JParams {
 
 #if defined(__CUDACC_RTC__) || defined(__CUDA_ARCH__)
 
+#ifndef __CUDACC_RTC__
+#include "exp_cr.cuh"
+#endif
+
 #define TTJ_THREADS 256
 
 __device__ __forceinline__ unsigned ttj_fdiv(unsigned n, const JFastDiv& f) { return (__umulhi(n, f.m) + n) >> f.s; }
 
 __device__ __forceinline__ float ttj_relu(float x) { return (0.0f < x) ? x : 0.0f; }
 
-// e^x rounded once from a double approximation with relative error below
-// 2^-44 (table-driven reduction, P. T. P. Tang, ACM TOMS 15(2), 1989: x =
-// (64 m + j) ln2/64 + r, |r| <= ln2/128, e^r by its degree-4 Taylor
-// polynomial), i.e. the correctly rounded float except within 2^-44 of a
-// rounding midpoint -- the same values as glibc's expf on all but ~0.07% of
-// inputs, where glibc is the one off by an ulp.
-__shared__ double ttj_exp2_tab[64];
+// sigmoid with the float-float exp of exp_cr.cuh (NVRTC receives that file's
+// text ahead of this one).
+__shared__ ExpCrTable ttj_exp_tab;
 
-__device__ __forceinline__ void ttj_exp_table_init() {
-    for (int i = threadIdx.x; i < 64; i += blockDim.x) ttj_exp2_tab[i] = exp2((double)i * (1.0 / 64.0));
-}
+__device__ __forceinline__ void ttj_exp_table_init() { exp_cr_table_init(ttj_exp_tab); }
 
-__device__ __forceinline__ float ttj_exp(float x) {
-    if (x != x) return x;
-    if (x > 89.0f) return __int_as_float(0x7f800000);
-    if (x < -104.0f) return 0.0f;
-    const int k = __float2int_rn(x * 92.33248261689366f);
-    const double r = fma(-(double)k, 0.010830424696249145, (double)x);
-    double p = fma(r, 1.0 / 24.0, 1.0 / 6.0);
-    p = fma(p, r, 0.5);
-    p = fma(p, r, 1.0);
-    p = fma(p, r, 1.0);
-    double e = p * ttj_exp2_tab[k & 63];
-    e = __longlong_as_double(__double_as_longlong(e) + (long long)(k >> 6) * (1ll << 52));
-    return __double2float_rn(e);
-}
-
-__device__ __forceinline__ float ttj_sigmoid(float x) { return 1.0f / (1.0f + ttj_exp(-x)); }
+__device__ __forceinline__ float ttj_sigmoid(float x) { return sigmoid_cr(x, ttj_exp_tab); }
 
 // Operand kinds: 0 full (contiguous columns), 1 row broadcast ([1,C]),
 // 2 column broadcast ([R,1]).

@@ -9,6 +9,9 @@
 #include <string>
 
 #include "../../include/tt_cuda.h"
+#ifdef __CUDACC__
+#include "exp_cr.cuh"
+#endif
 
 // ------------------------------------------------------------------ errors
 namespace ttc {
@@ -158,40 +161,16 @@ __device__ __forceinline__ void store_group(const DOutView& v, long long seg, lo
 
 __device__ __forceinline__ float op_relu(float x) { return (0.0f < x) ? x : 0.0f; }
 
-// exp for the sigmoid step, rounded once from a double approximation with
-// relative error below 2^-44, so the float result is the correctly rounded
-// e^x except within 2^-44 of a rounding midpoint. The CPU reference gets
-// e^x from glibc's expf (within 0.502 ulp), so both sides nearly always hold
-// the same float and the IEEE add and divide that follow match bit for bit;
-// a 2-ulp expf would put sigmoid up to 4 ulp away.
-// Method: table-driven reduction (P. T. P. Tang, "Table-driven implementation
-// of the exponential function in IEEE floating-point arithmetic", ACM TOMS
-// 15(2), 1989): x = (64 m + j) ln2/64 + r with |r| <= ln2/128, e^x =
-// 2^m * 2^(j/64) * e^r, e^r by its degree-4 Taylor polynomial (truncation
-// error < 4e-14 on that interval). The 2^(j/64) table lives in shared memory
-// (exp2_table_init fills it at kernel start).
-static __shared__ double s_exp2_tab[64];
+// sigmoid = 1 / (1 + e^-x) with the float-float exp of exp_cr.cuh; the
+// 2^(j/64) table lives in shared memory (exp2_table_init_block fills it at
+// kernel start, before a __syncthreads).
+static __shared__ ExpCrTable s_exp_tab;
 
-__device__ __forceinline__ void exp2_table_init_block() {
-    for (int i = threadIdx.x; i < 64; i += blockDim.x) s_exp2_tab[i] = exp2((double)i * (1.0 / 64.0));
-}
+__device__ __forceinline__ void exp2_table_init_block() { exp_cr_table_init(s_exp_tab); }
 
-__device__ __forceinline__ float exp_rn(float x) {
-    if (x != x) return x;
-    if (x > 89.0f) return __int_as_float(0x7f800000);  // overflows to +inf
-    if (x < -104.0f) return 0.0f;                      // below half the smallest subnormal
-    const int k = __float2int_rn(x * 92.33248261689366f);  // x * 64 / ln2
-    const double r = fma(-(double)k, 0.010830424696249145, (double)x);  // x - k ln2/64
-    double p = fma(r, 1.0 / 24.0, 1.0 / 6.0);
-    p = fma(p, r, 0.5);
-    p = fma(p, r, 1.0);
-    p = fma(p, r, 1.0);
-    double e = p * s_exp2_tab[k & 63];
-    e = __longlong_as_double(__double_as_longlong(e) + (long long)(k >> 6) * (1ll << 52));  // * 2^m
-    return __double2float_rn(e);
-}
+__device__ __forceinline__ float exp_rn(float x) { return exp_cr(x, s_exp_tab); }
 
-__device__ __forceinline__ float op_sigmoid(float x) { return 1.0f / (1.0f + exp_rn(-x)); }
+__device__ __forceinline__ float op_sigmoid(float x) { return sigmoid_cr(x, s_exp_tab); }
 
 // Applies f(g, w) to every element. Arithmetic runs on all groups (invalid
 // groups compute on zeros and are never stored or summed).

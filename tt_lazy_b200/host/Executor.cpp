@@ -290,31 +290,88 @@ bool is_contiguous(const Operand& o) {
 
 // Dense row-major copy of an operand (used only when a consumer cannot fold
 // the operand's strides).
+// Dense copy of a window whose innermost dim has stride 1: dims (outer...,
+// rows, cols) with strides (..., rs, 1) into dst (row-major). Dims before the
+// last two become chain segments (one launch per extra outer index).
+void copy_rows(const float* src, const std::vector<int64_t>& sh, const std::vector<int64_t>& st, float* dst) {
+    const int r = (int)sh.size();
+    const int64_t cols = sh[(size_t)r - 1], rows = r >= 2 ? sh[(size_t)r - 2] : 1;
+    const int64_t rs = r >= 2 ? st[(size_t)r - 2] : cols;
+    const int64_t nseg = r >= 3 ? sh[(size_t)r - 3] : 1, ss = r >= 3 ? st[(size_t)r - 3] : 0;
+    const int64_t outer = r >= 4 ? sh[0] : 1, os = r >= 4 ? st[0] : 0;
+    if (r > 4 || nseg > 65535 || rows > INT32_MAX || cols > INT32_MAX)
+        throw std::runtime_error("tt_lazy: view too large to densify");
+    for (int64_t o = 0; o < outer; ++o) {
+        ttc_chain_desc d;
+        std::memset(&d, 0, sizeof d);
+        d.rows = (int32_t)rows;
+        d.cols = (int32_t)cols;
+        d.nseg = (int32_t)nseg;
+        d.n_inputs = 1;
+        d.inputs[0] = ttc_in_view{src + o * os, rs, 1, ss};
+        d.n_outputs = 1;
+        d.outputs[0] = ttc_out_view{dst + o * nseg * rows * cols, cols, rows * cols};
+        d.n_instr = 2;
+        d.program[0] = ttc_instr{TTC_OP_LOAD, TTC_SRC_INPUT, 0, 0};
+        d.program[1] = ttc_instr{TTC_OP_STORE, TTC_SRC_ACC, 0, 0};
+        check(ttc_eltwise_chain(&d));
+    }
+}
+
+// Dense row-major copy of a strided view of rank <= 4 (transposes and split
+// chunks, and compositions of them): the innermost dim with stride 1 is
+// copied with 128-bit accesses; a view whose stride-1 dim is the
+// second-to-last (a transposed window) is packed that way and then
+// transposed by the tiled transpose kernel.
 Operand contiguous(const Operand& o) {
     if (is_contiguous(o)) return o;
     Operand r;
     r.shape = o.shape;
     r.view = new_buffer(o.shape);
-    const int rk = (int)o.shape.size();
-    if (rk != 2) throw std::runtime_error("tt_lazy: cannot densify a strided view of rank != 2");
-    const int64_t rows = o.shape[0], cols = o.shape[1];
-    const int64_t rs = o.view.strides[0], cs = o.view.strides[1];
-    if (cs == 1) {
-        check(ttc_copy2d(o.view.ptr(), rs, r.view.ptr(), cols, rows, cols));
-    } else if (rs == 1) {
-        if (cs == rows) {
-            check(ttc_transpose(o.view.ptr(), r.view.ptr(), 1, cols, rows));
+    // collapse dims of size 1 and dims whose strides nest
+    std::vector<int64_t> sh, st;
+    for (size_t i = 0; i < o.shape.size(); ++i) {
+        if (o.shape[i] == 1) continue;
+        const int64_t n = o.shape[i], s = o.view.strides[i];
+        if (!sh.empty() && st.back() == n * s) {
+            sh.back() *= n;
+            st.back() = s;
         } else {
-            DeviceView packed = new_buffer({(uint32_t)cols, (uint32_t)rows});
-            check(ttc_copy2d(o.view.ptr(), cs, packed.ptr(), rows, cols, rows));
-            check(ttc_transpose(packed.ptr(), r.view.ptr(), 1, cols, rows));
+            sh.push_back(n);
+            st.push_back(s);
         }
+    }
+    const size_t k = sh.size();
+    if (k >= 1 && st[k - 1] == 1) {
+        copy_rows(o.view.ptr(), sh, st, r.view.ptr());
+    } else if (k >= 2 && st[k - 2] == 1) {
+        // pack as [..., cols, rows] (stride 1 innermost), then transpose the last two dims
+        std::vector<int64_t> psh = sh, pst = st;
+        std::swap(psh[k - 1], psh[k - 2]);
+        std::swap(pst[k - 1], pst[k - 2]);
+        int64_t batch = 1;
+        for (size_t i = 0; i + 2 < k; ++i) batch *= sh[i];
+        DeviceView packed = new_buffer({(uint32_t)(batch * psh[k - 2]), (uint32_t)psh[k - 1]});
+        copy_rows(o.view.ptr(), psh, pst, packed.ptr());
+        check(ttc_transpose(packed.ptr(), r.view.ptr(), batch, psh[k - 2], psh[k - 1]));
     } else {
-        throw std::runtime_error("tt_lazy: cannot densify a view with strides (" + std::to_string(rs) + ", " +
-                                 std::to_string(cs) + ")");
+        std::string s;
+        for (size_t i = 0; i < o.shape.size(); ++i) s += (i ? ", " : "") + std::to_string(o.view.strides[i]);
+        throw std::runtime_error("tt_lazy: cannot densify a view with strides (" + s + ")");
     }
     return r;
 }
+
+}  // namespace
+
+DeviceView tt_lazy::dense_view(const DeviceView& v, const std::vector<uint32_t>& shape) {
+    Operand o;
+    o.view = v;
+    o.shape = shape;
+    return contiguous(o).view;
+}
+
+namespace {
 
 // --------------------------------------------------------- program builder
 // Lowers a member DAG (element-wise ops over one element space, optional tail

@@ -106,6 +106,10 @@ class MemoryManager {
 DeviceView upload(const Tensor& t);
 void clear_constant_cache();
 
+// Dense row-major device copy of a strided view (rank <= 4) of `shape`; the
+// view itself when it is already dense.
+DeviceView dense_view(const DeviceView& v, const std::vector<uint32_t>& shape);
+
 class EvaluationManager {
    public:
     virtual ~EvaluationManager() = default;

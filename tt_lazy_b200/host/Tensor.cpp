@@ -170,33 +170,9 @@ void Tensor::copy_from_device() {
             throw std::runtime_error(ttc_last_error());
         return;
     }
-    // rank <= 2 strided view: copy rows (or columns of a transposed view) on device.
-    const int64_t rows = r >= 2 ? shape_[r - 2] : 1, cols = shape_[r - 1];
-    const int64_t batch = (int64_t)(numel_ / (rows * cols));
-    auto tmp = tt_lazy::MemoryManager::instance().allocate(numel_ * sizeof(float));
-    const int64_t rs = r >= 2 ? device_.strides[r - 2] : cols, cs = device_.strides[r - 1];
-    const int64_t bs = r >= 3 ? device_.strides[r - 3] : rows * cols;
-    for (int64_t b = 0; b < batch; ++b) {
-        const float* src = device_.ptr() + b * bs;
-        float* dst = tmp->ptr() + b * rows * cols;
-        int rc;
-        if (cs == 1) {
-            rc = ttc_copy2d(src, rs, dst, cols, rows, cols);
-        } else if (rs == 1) {
-            // transposed view: element (i, j) at src[j * cs + i], i.e. the
-            // physical matrix is [cols, rows] with row pitch cs.
-            if (cs == rows) {
-                rc = ttc_transpose(src, dst, 1, cols, rows);
-            } else {
-                auto packed = tt_lazy::MemoryManager::instance().allocate((size_t)rows * cols * sizeof(float));
-                rc = ttc_copy2d(src, cs, packed->ptr(), rows, cols, rows);
-                if (rc == TTC_OK) rc = ttc_transpose(packed->ptr(), dst, 1, cols, rows);
-            }
-        } else
-            throw std::runtime_error("materialising a view with strides that are neither row nor column major");
-        if (rc != TTC_OK) throw std::runtime_error(ttc_last_error());
-    }
-    if (ttc_memcpy_d2h(data_.get(), tmp->ptr(), numel_ * sizeof(float)) != TTC_OK)
+    // strided view (transpose / split chunk): densify on the device, then one copy
+    const DeviceView dense = tt_lazy::dense_view(device_, shape_vector());
+    if (ttc_memcpy_d2h(data_.get(), dense.ptr(), numel_ * sizeof(float)) != TTC_OK)
         throw std::runtime_error(ttc_last_error());
 }
 
