@@ -195,6 +195,13 @@ int ttc_eltwise_chain(const ttc_chain_desc* desc);
  * ttc_eltwise_chain to rounding, not bit for bit, when a reduction is fused. */
 int ttc_eltwise_chain_noalloc(const ttc_chain_desc* desc);
 
+/* Diagnostics (no reference counterpart): the CUDA source text that the
+ * program-specialised chain kernel for `desc` is compiled from (NVRTC, at
+ * first use). Writes at most cap - 1 characters and a terminating NUL to
+ * `out` (may be NULL to query the length) and the full length to *len.
+ * Needs no device and no ttc_init. */
+int ttc_chain_jit_source(const ttc_chain_desc* desc, char* out, size_t cap, size_t* len);
+
 /* ------------------------------------------------------------ reductions
  * math::reduce_sum (src/backend/cpu/reduce_sum.cpp:9-62) and the MEAN type
  * of ReduceArgs (src/frontend/operations.hpp:13-14) over any set of dims of a

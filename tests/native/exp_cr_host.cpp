@@ -19,7 +19,7 @@
 struct Dim {
     unsigned x;
 };
-static const Dim threadIdx{0}, blockDim{1};
+static Dim threadIdx{0}, blockDim{1};
 static inline float __fmaf_rn(float a, float b, float c) { return std::fma(a, b, c); }
 static inline float __fadd_rn(float a, float b) { return a + b; }
 static inline float __fsub_rn(float a, float b) { return a - b; }
@@ -56,12 +56,7 @@ using std::fma;
 int main(int argc, char** argv) {
     const long long stride = argc > 1 ? std::atoll(argv[1]) : 1;
     ExpCrTable tab;
-    exp_cr_table_init(tab);
-    for (int i = 1; i < 64; ++i) {  // the loop above ran with one "thread"
-        const double v = std::exp2((double)i / 64.0);
-        tab.hi[i] = (float)v;
-        tab.lo[i] = (float)(v - (double)tab.hi[i]);
-    }
+    exp_cr_table_init(tab);  // one "thread" of a one-thread block fills every entry
     const long long top = __float_as_int(104.0f);
     long long n = 0, bad = 0, over1 = 0;
 #pragma omp parallel for reduction(+ : n, bad, over1) schedule(dynamic, 4096)

@@ -70,7 +70,7 @@ class MemoryStats(C.Structure):
 EXPORTS = ["ttc_last_error", "ttc_init", "ttc_shutdown", "ttc_device_count", "ttc_version", "ttc_get_stream",
            "ttc_set_stream", "ttc_synchronize", "ttc_malloc", "ttc_free", "ttc_memcpy_h2d", "ttc_memcpy_d2h",
            "ttc_memcpy_d2d", "ttc_memset_zero", "ttc_host_alloc", "ttc_host_free", "ttc_get_memory_stats",
-           "ttc_eltwise_chain", "ttc_eltwise_chain_noalloc", "ttc_reduce", "ttc_transpose", "ttc_copy2d", "ttc_gemm", "ttc_gemm_select_path",
+           "ttc_eltwise_chain", "ttc_eltwise_chain_noalloc", "ttc_chain_jit_source", "ttc_reduce", "ttc_transpose", "ttc_copy2d", "ttc_gemm", "ttc_gemm_select_path",
            "ttc_comm_unique_id", "ttc_comm_init", "ttc_allreduce_sum", "ttc_comm_destroy"]
 
 
@@ -102,6 +102,7 @@ def lib():
         L.ttc_set_stream.argtypes = [C.c_void_p]
         L.ttc_eltwise_chain.argtypes = [C.POINTER(ChainDesc)]
         L.ttc_eltwise_chain_noalloc.argtypes = [C.POINTER(ChainDesc)]
+        L.ttc_chain_jit_source.argtypes = [C.POINTER(ChainDesc), C.c_char_p, C.c_size_t, C.POINTER(C.c_size_t)]
         L.ttc_gemm.argtypes = [C.POINTER(GemmDesc)]
         L.ttc_gemm_select_path.argtypes = [C.POINTER(GemmDesc)]
         L.ttc_reduce.argtypes = [C.c_void_p, C.POINTER(C.c_uint32), C.c_int, C.POINTER(C.c_int32), C.c_int,
@@ -225,6 +226,15 @@ def chain_desc(rows, cols, inputs, outputs, program, reduce=REDUCE_NONE, reduce_
 
 def eltwise_chain(desc):
     check(lib().ttc_eltwise_chain(C.byref(desc)))
+
+
+def chain_jit_source(desc):
+    """CUDA source of the specialised kernel for `desc` (no device needed)."""
+    n = C.c_size_t(0)
+    check(lib().ttc_chain_jit_source(C.byref(desc), None, 0, C.byref(n)))
+    buf = C.create_string_buffer(n.value + 1)
+    check(lib().ttc_chain_jit_source(C.byref(desc), buf, n.value + 1, C.byref(n)))
+    return buf.value.decode()
 
 
 def gemm(M, N, K, a, lda, b, ldb, c=None, ldc=0, trans_a=False, trans_b=False, path=GEMM_AUTO, epilogue=None):

@@ -54,13 +54,16 @@ __device__ __forceinline__ unsigned ttj_fdiv(unsigned n, const JFastDiv& f) { re
 
 __device__ __forceinline__ float ttj_relu(float x) { return (0.0f < x) ? x : 0.0f; }
 
-// sigmoid with the float-float exp of exp_cr.cuh (NVRTC receives that file's
-// text ahead of this one).
+// sigmoid with the exp of exp_cr.cuh (NVRTC receives that file's text ahead
+// of this one): one range test for all G*W values of a thread.
 __shared__ ExpCrTable ttj_exp_tab;
 
 __device__ __forceinline__ void ttj_exp_table_init() { exp_cr_table_init(ttj_exp_tab); }
 
-__device__ __forceinline__ float ttj_sigmoid(float x) { return sigmoid_cr(x, ttj_exp_tab); }
+template <int G, int W>
+__device__ __forceinline__ void ttj_sigmoid_all(float (&acc)[G][W]) {
+    sigmoid_cr_n<G * W>(&acc[0][0], ttj_exp_tab);
+}
 
 // Operand kinds: 0 full (contiguous columns), 1 row broadcast ([1,C]),
 // 2 column broadcast ([R,1]).
@@ -101,6 +104,34 @@ __device__ __forceinline__ float ttj_warp_sum(float v) {
 }
 
 // ---------------------------------------------------------------- kernels
+// Software pipelining: every kernel issues the loads of its next iteration
+// (Body::load into a second register buffer) before it computes the current
+// one (Body::run), so the memory latency of the next tile hides behind the
+// arithmetic of this one. Summation order per thread is the plain loop's.
+template <class Body, int G, int W>
+__device__ __forceinline__ void ttj_copy_buf(float (&dst)[Body::NB][G][W], const float (&src)[Body::NB][G][W]) {
+#pragma unroll
+    for (int b = 0; b < Body::NB; ++b)
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int w = 0; w < W; ++w) dst[b][g][w] = src[b][g][w];
+}
+
+template <int W, int G>
+__device__ __forceinline__ void ttj_flat_index(const JParams& p, unsigned blk, unsigned (&row)[G], unsigned (&col)[G],
+                                               bool (&valid)[G]) {
+    const unsigned q0 = blk * (TTJ_THREADS * G) + threadIdx.x;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const unsigned q = q0 + g * TTJ_THREADS;
+        valid[g] = q < p.total;
+        const unsigned r = ttj_fdiv(q, p.cpr_div);
+        row[g] = r;
+        col[g] = (q - r * p.cpr) * W;
+    }
+}
+
 template <int W, int G, bool SIG, bool REDUCE_ALL, class Body>
 __device__ __forceinline__ void ttj_flat(const JParams& p) {
     if (SIG) {
@@ -109,20 +140,21 @@ __device__ __forceinline__ void ttj_flat(const JParams& p) {
     }
     const long long seg = blockIdx.y;
     float sum = 0.0f;
-    for (unsigned blk = blockIdx.x; (unsigned long long)blk * (TTJ_THREADS * G) < p.total; blk += gridDim.x) {
-        const unsigned q0 = blk * (TTJ_THREADS * G) + threadIdx.x;
-        long long row[G], col[G];
-        bool valid[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const unsigned q = q0 + g * TTJ_THREADS;
-            valid[g] = q < p.total;
-            const unsigned r = ttj_fdiv(q, p.cpr_div);
-            row[g] = r;
-            col[g] = (long long)(q - r * p.cpr) * W;
-        }
+    unsigned blk = blockIdx.x;
+    unsigned row[G], col[G];
+    bool valid[G];
+    ttj_flat_index<W, G>(p, blk, row, col, valid);
+    float buf[Body::NB][G][W];
+    Body::load(p, buf, seg, row, col, valid);
+    while ((unsigned long long)blk * (TTJ_THREADS * G) < p.total) {
+        const unsigned nblk = blk + gridDim.x;
+        unsigned nrow[G], ncol[G];
+        bool nvalid[G];
+        ttj_flat_index<W, G>(p, nblk, nrow, ncol, nvalid);
+        float nbuf[Body::NB][G][W];
+        Body::load(p, nbuf, seg, nrow, ncol, nvalid);
         float acc[G][W];
-        Body::run(p, acc, seg, row, col, valid);
+        Body::run(p, acc, buf, seg, row, col, valid);
         if (REDUCE_ALL) {
 #pragma unroll
             for (int g = 0; g < G; ++g)
@@ -130,6 +162,14 @@ __device__ __forceinline__ void ttj_flat(const JParams& p) {
 #pragma unroll
                     for (int w = 0; w < W; ++w) sum += acc[g][w];
         }
+        blk = nblk;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            row[g] = nrow[g];
+            col[g] = ncol[g];
+            valid[g] = nvalid[g];
+        }
+        ttj_copy_buf<Body, G, W>(buf, nbuf);
     }
     if (REDUCE_ALL) {
         __shared__ float red[TTJ_THREADS / 32];
@@ -144,6 +184,21 @@ __device__ __forceinline__ void ttj_flat(const JParams& p) {
     }
 }
 
+// Row sums: a warp per row, lanes across the row's column quads; the walk
+// over (row, column block) pairs is flattened so the prefetch crosses rows.
+template <int W, int G>
+__device__ __forceinline__ void ttj_rows_index(const JParams& p, unsigned r, unsigned c0, unsigned (&row)[G],
+                                               unsigned (&col)[G], bool (&valid)[G]) {
+    const unsigned lane = threadIdx.x & 31;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        const unsigned ch = c0 + lane + g * 32;
+        valid[g] = r < (unsigned)p.rows && ch < p.cpr;
+        row[g] = r;
+        col[g] = ch * W;
+    }
+}
+
 template <int W, int G, bool SIG, class Body>
 __device__ __forceinline__ void ttj_rows(const JParams& p) {
     if (SIG) {
@@ -152,30 +207,59 @@ __device__ __forceinline__ void ttj_rows(const JParams& p) {
     }
     const long long seg = blockIdx.y;
     const int lane = threadIdx.x & 31;
-    const unsigned warp = (blockIdx.x * TTJ_THREADS + threadIdx.x) >> 5;
     const unsigned nwarps = (gridDim.x * TTJ_THREADS) >> 5;
-    for (unsigned r = warp; r < (unsigned)p.rows; r += nwarps) {
-        float sum = 0.0f;
-        for (unsigned c0 = lane; c0 < p.cpr; c0 += 32 * G) {
-            long long row[G], col[G];
-            bool valid[G];
-#pragma unroll
-            for (int g = 0; g < G; ++g) {
-                const unsigned ch = c0 + g * 32;
-                valid[g] = ch < p.cpr;
-                row[g] = r;
-                col[g] = (long long)ch * W;
-            }
-            float acc[G][W];
-            Body::run(p, acc, seg, row, col, valid);
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-                if (valid[g])
-#pragma unroll
-                    for (int w = 0; w < W; ++w) sum += acc[g][w];
+    unsigned r = (blockIdx.x * TTJ_THREADS + threadIdx.x) >> 5;
+    unsigned c0 = 0;  // warp-uniform column-quad base of this step
+    unsigned row[G], col[G];
+    bool valid[G];
+    ttj_rows_index<W, G>(p, r, c0, row, col, valid);
+    float buf[Body::NB][G][W];
+    Body::load(p, buf, seg, row, col, valid);
+    float sum = 0.0f;
+    while (r < (unsigned)p.rows) {
+        unsigned nc0 = c0 + 32 * G, nr = r;
+        if (nc0 >= p.cpr) {
+            nc0 = 0;
+            nr = r + nwarps;
         }
-        sum = ttj_warp_sum(sum);
-        if (lane == 0) p.red_out[seg * p.red_sseg + r] = p.mean ? (float)((double)sum / p.count) : sum;
+        unsigned nrow[G], ncol[G];
+        bool nvalid[G];
+        ttj_rows_index<W, G>(p, nr, nc0, nrow, ncol, nvalid);
+        float nbuf[Body::NB][G][W];
+        Body::load(p, nbuf, seg, nrow, ncol, nvalid);
+        float acc[G][W];
+        Body::run(p, acc, buf, seg, row, col, valid);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+            if (valid[g])
+#pragma unroll
+                for (int w = 0; w < W; ++w) sum += acc[g][w];
+        if (nr != r) {  // row finished (warp-uniform)
+            sum = ttj_warp_sum(sum);
+            if (lane == 0) p.red_out[seg * p.red_sseg + r] = p.mean ? (float)((double)sum / p.count) : sum;
+            sum = 0.0f;
+        }
+        r = nr;
+        c0 = nc0;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            row[g] = nrow[g];
+            col[g] = ncol[g];
+            valid[g] = nvalid[g];
+        }
+        ttj_copy_buf<Body, G, W>(buf, nbuf);
+    }
+}
+
+template <int W, int G>
+__device__ __forceinline__ void ttj_cols_index(int r, int r1, unsigned ch, bool col_ok, unsigned (&row)[G],
+                                               unsigned (&col)[G], bool (&valid)[G]) {
+    const int NW = TTJ_THREADS / 32;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+        row[g] = (unsigned)(r + g * NW);
+        col[g] = ch * W;
+        valid[g] = col_ok && r + g * NW < r1;
     }
 }
 
@@ -196,22 +280,32 @@ __device__ __forceinline__ void ttj_cols(const JParams& p) {
     float s[W];
 #pragma unroll
     for (int w = 0; w < W; ++w) s[w] = 0.0f;
-    for (int r = r0 + warp; r < r1; r += NW * G) {
-        long long row[G], col[G];
-        bool valid[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            row[g] = r + g * NW;
-            col[g] = (long long)ch * W;
-            valid[g] = col_ok && row[g] < r1;
-        }
+    int r = r0 + warp;
+    unsigned row[G], col[G];
+    bool valid[G];
+    ttj_cols_index<W, G>(r, r1, ch, col_ok, row, col, valid);
+    float buf[Body::NB][G][W];
+    Body::load(p, buf, seg, row, col, valid);
+    for (; r < r1; r += NW * G) {
+        unsigned nrow[G], ncol[G];
+        bool nvalid[G];
+        ttj_cols_index<W, G>(r + NW * G, r1, ch, col_ok, nrow, ncol, nvalid);
+        float nbuf[Body::NB][G][W];
+        Body::load(p, nbuf, seg, nrow, ncol, nvalid);
         float acc[G][W];
-        Body::run(p, acc, seg, row, col, valid);
+        Body::run(p, acc, buf, seg, row, col, valid);
 #pragma unroll
         for (int g = 0; g < G; ++g)
             if (valid[g])
 #pragma unroll
                 for (int w = 0; w < W; ++w) s[w] += acc[g][w];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            row[g] = nrow[g];
+            col[g] = ncol[g];
+            valid[g] = nvalid[g];
+        }
+        ttj_copy_buf<Body, G, W>(buf, nbuf);
     }
     __shared__ float sm[TTJ_THREADS / 32][32 * W + 1];
 #pragma unroll

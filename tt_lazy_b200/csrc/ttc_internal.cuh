@@ -161,16 +161,12 @@ __device__ __forceinline__ void store_group(const DOutView& v, long long seg, lo
 
 __device__ __forceinline__ float op_relu(float x) { return (0.0f < x) ? x : 0.0f; }
 
-// sigmoid = 1 / (1 + e^-x) with the float-float exp of exp_cr.cuh; the
-// 2^(j/64) table lives in shared memory (exp2_table_init_block fills it at
-// kernel start, before a __syncthreads).
+// sigmoid = 1 / (1 + e^-x) with the exp of exp_cr.cuh; its 2^(j/64) table
+// lives in shared memory (exp2_table_init_block fills it at kernel start,
+// before a __syncthreads).
 static __shared__ ExpCrTable s_exp_tab;
 
 __device__ __forceinline__ void exp2_table_init_block() { exp_cr_table_init(s_exp_tab); }
-
-__device__ __forceinline__ float exp_rn(float x) { return exp_cr(x, s_exp_tab); }
-
-__device__ __forceinline__ float op_sigmoid(float x) { return sigmoid_cr(x, s_exp_tab); }
 
 // Applies f(g, w) to every element. Arithmetic runs on all groups (invalid
 // groups compute on zeros and are never stored or summed).
@@ -219,7 +215,10 @@ __device__ __forceinline__ void run_program_io(const DProgram& P, float (&acc)[G
                     if (io.ok(g)) io.load(a, g, acc[g]);
                 break;
             case D_RELU: each<G, W>([&](int g, int w) { acc[g][w] = op_relu(acc[g][w]); }); break;
-            case D_SIGMOID: each<G, W>([&](int g, int w) { acc[g][w] = op_sigmoid(acc[g][w]); }); break;
+            case D_SIGMOID:
+#pragma unroll
+                for (int g = 0; g < G; ++g) sigmoid_cr_n<W>(acc[g], s_exp_tab);
+                break;
             case D_ADD_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + acc[g][w]; }); break;
             case D_MUL_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * acc[g][w]; }); break;
             case D_ADD_IN:
