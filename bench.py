@@ -51,53 +51,64 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling of SM clocks and throttle reasons while timing."""
+    """SM clock and throttle-reason samples of this process's GPU taken while
+    the timed region runs: NVML read every 2 ms from a background thread (the
+    GPU is found by its PCI bus id, so CUDA_VISIBLE_DEVICES does not matter).
+    Only reads; changes nothing."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
 
     def __init__(self, device):
         self.device = device
-        self.proc = None
+        self.samples, self.max_mhz, self.reasons = [], None, set()
+        self.error = None
 
     def __enter__(self):
+        self.stop = threading.Event()
+        self.thread = None
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.device), "--query-gpu=" + self.Q,
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except Exception:
-            self.proc = None
+            import pynvml as nv
+            import torch
+
+            nv.nvmlInit()
+            p = torch.cuda.get_device_properties(self.device)
+            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+            self.h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.nv = nv
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+        except Exception as e:  # noqa: BLE001
+            self.error = repr(e)
         return self
 
-    def __exit__(self, *exc):
-        self.lines = []
-        if self.proc:
-            self.proc.terminate()
+    def _poll(self):
+        nv = self.nv
+        while not self.stop.is_set():
             try:
-                out, _ = self.proc.communicate(timeout=5)
-                self.lines = [l for l in out.splitlines() if l.strip()]
-            except Exception:
-                self.proc.kill()
+                self.samples.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+                bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for name, const in self.REASONS:
+                    if bits & getattr(nv, const):
+                        self.reasons.add(name)
+            except Exception as e:  # noqa: BLE001
+                self.error = repr(e)
+                return
+            time.sleep(0.002)
+
+    def __exit__(self, *exc):
+        self.stop.set()
+        if self.thread:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0, "error": self.error}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml, 2 ms"}
 
 
 # ------------------------------------------------------------------ helpers
@@ -117,14 +128,33 @@ def pinned(shape, capi):
     return np.ctypeslib.as_array(buf).reshape(shape), p.value
 
 
+X_BLOCK = 8192  # X is generated in seeded row blocks, so a shard is the same rows at every world size
+
+
 def make_inputs(rank, world):
+    from tt_lazy_b200 import shard
+
     rng = np.random.default_rng(2)
     W1 = (rng.standard_normal((K1, N1), dtype=np.float32) / np.float32(np.sqrt(K1)))
     W2 = (rng.standard_normal((N1, K1), dtype=np.float32) / np.float32(np.sqrt(N1)))
-    rows = M_GLOBAL // world
-    xr = np.random.default_rng(1000 + 2 * 97 + rank)  # seed 2, one stream per shard
-    X = xr.standard_normal((rows, K1), dtype=np.float32)
+    a, b = shard.row_range(M_GLOBAL, world, rank)
+    X = np.empty((b - a, K1), np.float32)
+    for blk in range(a // X_BLOCK, (b + X_BLOCK - 1) // X_BLOCK):
+        rows = np.random.default_rng(2000 + blk).standard_normal((X_BLOCK, K1), dtype=np.float32)
+        lo, hi = max(a, blk * X_BLOCK), min(b, (blk + 1) * X_BLOCK)
+        X[lo - a:hi - a] = rows[lo - blk * X_BLOCK:hi - blk * X_BLOCK]
     return X, W1, W2
+
+
+def chain_rows(chunks):
+    """Rows of A[16384, 16384] ~ U(-1,1) that split chunks `chunks` of
+    transpose(A) read (chunk i = rows 2048 i .. 2048 i + 2047), each chunk's
+    rows from its own seeded stream (seed 3)."""
+    out = np.empty((len(chunks) * CHAIN_SPLIT, CHAIN_N), np.float32)
+    for j, c in enumerate(chunks):
+        out[j * CHAIN_SPLIT:(j + 1) * CHAIN_SPLIT] = np.random.default_rng(3000 + c).uniform(
+            -1, 1, (CHAIN_SPLIT, CHAIN_N)).astype(np.float32)
+    return out
 
 
 # ------------------------------------------------------------- CPU baseline
@@ -218,10 +248,9 @@ def run_ours(args):
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-        uid = tl.comm_unique_id() if rank == 0 else None
-        obj = [uid]
-        dist.broadcast_object_list(obj, src=0)
-        tl.comm_init(world, rank, obj[0], 60000)
+        from tt_lazy_b200 import shard
+
+        shard.init_comm(world, rank, 60000)
     stream = torch.cuda.ExternalStream(tl.stream())
 
     def barrier():
@@ -252,8 +281,8 @@ def run_ours(args):
         plan.run()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
     with Clocks(local) as clk:
-        barrier()
         e0.record(stream)
         for _ in range(args.steps):
             plan.run()
@@ -322,11 +351,15 @@ def run_ours(args):
             traffic = None
     del Xd, W1d, Hd
 
-    # ---- bandwidth graph (eltwise chain block)
+    # ---- bandwidth graph (eltwise chain block): chunk i of the split on the
+    # rank that owns it, which holds only the rows of A its chunks read; no
+    # collective (strong scaling over the 8 chunks)
     chain = None
     if not args.skip_chain:
-        rng = np.random.default_rng(3)
-        A = rng.uniform(-1, 1, (CHAIN_N, CHAIN_N)).astype(np.float32)
+        from tt_lazy_b200 import shard
+
+        mine = shard.owned_chunks(CHAIN_N // CHAIN_SPLIT, world, rank)
+        A = chain_rows(mine)
         T = tl.transpose(tl.constant(A))
         outs = [tl.reduce_sum(tl.multiply(tl.sigmoid(ch), tl.relu(tl.add(ch, ch))), [1])
                 for ch in tl.split(T, CHAIN_SPLIT, 1)]
@@ -342,15 +375,16 @@ def run_ours(args):
         c1.record(stream)
         barrier()
         cms = max_over_ranks(c0.elapsed_time(c1) / creps)
-        gbs = CHAIN_BYTES / (cms * 1e-3) / 1e9
+        gbs = CHAIN_BYTES / (cms * 1e-3) / 1e9  # whole job: all 8 chunks / slowest rank
+        per_gpu = gbs / world
         launches += cplan.kernels_last_run * (creps + 3)
-        chain = {"metric": "eltwise-chain HBM GB/s", "value": gbs * world, "unit": "GB/s", "per_gpu": gbs,
-                 "ms_per_step": cms, "kernels_per_step": cplan.kernels_last_run,
+        chain = {"metric": "eltwise-chain HBM GB/s", "value": gbs, "unit": "GB/s", "per_gpu": per_gpu,
+                 "ms_per_step": cms, "kernels_per_step": cplan.kernels_last_run, "scaling": "strong",
                  "workload": "A[16384,16384] U(-1,1) seed 3: transpose -> 8 column chunks -> "
-                             "sigmoid(C)*relu(C+C) -> reduce_sum dim 1 (replica per GPU)",
-                 "algorithmic_bytes": CHAIN_BYTES,
-                 "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak, "unit": "GB/s",
-                              "frac": gbs / hbm_peak, "peak_source": peak_kind}}
+                             "sigmoid(C)*relu(C+C) -> reduce_sum dim 1; chunks sharded over ranks",
+                 "chunks_per_gpu": len(mine), "algorithmic_bytes": CHAIN_BYTES,
+                 "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": hbm_peak, "unit": "GB/s",
+                              "frac": per_gpu / hbm_peak, "peak_source": peak_kind}}
         del cplan, outs
 
     # ---- CPU baseline (rank 0, N = 1 only)
@@ -398,7 +432,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-chain", action="store_true")

@@ -32,3 +32,29 @@ def test_calls_before_init_return_status():
     d = capi.ChainDesc()
     assert L.ttc_eltwise_chain(C.byref(d)) == capi.ERR_NOT_INIT
     assert L.ttc_version() >= 1
+
+
+def test_injected_comm_faults_return_an_error_status(monkeypatch):
+    """A failing communicator call (faked on the host, before NCCL or the GPU
+    is touched) comes back as TTC_ERR_NCCL with a message, not a crash."""
+    L = capi.lib()
+    uid = bytes(128)
+    monkeypatch.setenv("TTC_COMM_FAULT", "init")
+    assert L.ttc_comm_init(2, 0, uid, 1000) == 6
+    assert b"injected" in L.ttc_last_error()
+    monkeypatch.setenv("TTC_COMM_FAULT", "allreduce")
+    assert L.ttc_allreduce_sum(None, 0, 1000) == 6
+    assert b"injected" in L.ttc_last_error()
+    monkeypatch.delenv("TTC_COMM_FAULT")
+    assert L.ttc_allreduce_sum(None, 0, 1000) == capi.ERR_NOT_INIT  # no communicator
+
+
+def test_chain_jit_source_needs_no_device():
+    I = capi.instr
+    d = capi.chain_desc(64, 64, [capi.in_view(0x1000, 64)], [capi.out_view(0x2000, 64)],
+                        [I(capi.OP_LOAD, idx=0), I(capi.OP_SIGMOID), I(capi.OP_STORE, idx=0)])
+    src = capi.chain_jit_source(d)
+    assert "ttj_sigmoid_all" in src and "ttj_flat<W, G, true, false, Body>" in src
+    bad = capi.chain_desc(64, 64, [], [], [I(capi.OP_LOAD, idx=3)])
+    n = C.c_size_t()
+    assert capi.lib().ttc_chain_jit_source(C.byref(bad), None, 0, C.byref(n)) == 1

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 
 #include <chrono>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 
@@ -18,6 +19,16 @@
 namespace ttc {
 int set_error(int code, const char* fmt, ...);
 }
+
+namespace {
+// Host-side fault injection for the failure-handling tests: with
+// TTC_COMM_FAULT=init (or allreduce) set, that call fails with TTC_ERR_NCCL
+// before it touches NCCL or the GPU, as a failing library call would.
+bool inject_fault(const char* call) {
+    const char* e = std::getenv("TTC_COMM_FAULT");
+    return e && std::strcmp(e, call) == 0;
+}
+}  // namespace
 
 #if TTC_HAVE_NCCL
 #include <nccl.h>
@@ -63,6 +74,7 @@ int ttc_comm_unique_id(uint8_t out[TTC_UNIQUE_ID_BYTES]) {
 }
 
 int ttc_comm_init(int nranks, int rank, const uint8_t id[TTC_UNIQUE_ID_BYTES], int timeout_ms) {
+    if (inject_fault("init")) return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: injected communicator init fault");
     if (g_comm) return ttc::set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: communicator already initialised");
     if (nranks < 1 || rank < 0 || rank >= nranks || !id || timeout_ms <= 0)
         return ttc::set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: comm_init(nranks=%d, rank=%d, timeout=%d)", nranks,
@@ -80,6 +92,7 @@ int ttc_comm_init(int nranks, int rank, const uint8_t id[TTC_UNIQUE_ID_BYTES], i
 }
 
 int ttc_allreduce_sum(float* buf, size_t count, int timeout_ms) {
+    if (inject_fault("allreduce")) return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: injected all-reduce fault");
     if (!g_comm) return ttc::set_error(TTC_ERR_NOT_INITIALIZED, "tt_cuda: ttc_comm_init() not called");
     if (!buf && count) return ttc::set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: allreduce buffer is NULL");
     cudaStream_t st = (cudaStream_t)ttc_get_stream();

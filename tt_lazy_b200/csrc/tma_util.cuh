@@ -1,8 +1,9 @@
 // tma_util.cuh -- TMA tensor maps, mbarriers and bounded waits shared by the
 // TMA-fed kernels (the tcgen05 GEMM and the staged element-wise chain).
 //
-// No load here carries .multicast::cluster: these kernels run on every rank
-// of a multi-GPU job and only ever read this GPU's own memory.
+// Every TMA load here targets one CTA's own shared memory (no cluster-wide
+// delivery): these kernels run on every rank of a multi-GPU job and only
+// ever read this GPU's own memory.
 #pragma once
 #include <cuda.h>
 

@@ -1,0 +1,80 @@
+"""Small, self-contained launches of the hot kernels for profiling.
+
+    python -m tt_lazy_b200.prof gemm [M]      # tf32_gemm_kernel: X[M,4096] . W[4096,16384], 3 launches
+    python -m tt_lazy_b200.prof chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
+
+NAME: copy | readme (relu -> add -> multiply, stored, summed) | sigmoid |
+segments (sigmoid(C) * relu(C + C) over 8 row segments, column sums).
+Inputs are seeded, device-resident and larger than L2 at the default sizes;
+nothing is timed here (profile with ncu, time with bench.py).
+"""
+from __future__ import annotations
+
+import sys
+
+
+def _setup():
+    import torch
+
+    from tt_lazy_b200 import capi as ttc
+
+    ttc.init(0)
+    s = torch.cuda.Stream()
+    torch.cuda.set_stream(s)
+    ttc.check(ttc.lib().ttc_set_stream(ttc.C.c_void_p(s.cuda_stream)))
+    return torch, ttc
+
+
+def gemm(M=8192, N=16384, K=4096, reps=3):
+    torch, ttc = _setup()
+    g = torch.Generator(device="cuda").manual_seed(2)
+    a = torch.randn(M, K, device="cuda", generator=g)
+    b = torch.randn(K, N, device="cuda", generator=g) / 64
+    c = torch.empty(M, N, device="cuda")
+    for _ in range(reps):
+        ttc.gemm(M, N, K, a.data_ptr(), K, b.data_ptr(), N, c.data_ptr(), N, path=ttc.GEMM_TF32)
+    torch.cuda.synchronize()
+    print(f"gemm {M}x{N}x{K} ok, c[0,0] = {float(c[0, 0]):.6g}")
+
+
+def chain(name="segments", N=8192, reps=3):
+    torch, ttc = _setup()
+    I = ttc.instr
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.rand(N, N, device="cuda", generator=g) * 2 - 1
+    w = torch.empty_like(x)
+    s = torch.empty(8, N, device="cuda")
+    if name == "segments":
+        prog = [I(ttc.OP_LOAD, idx=0), I(ttc.OP_ADD, ttc.SRC_ACC), I(ttc.OP_RELU), I(ttc.OP_SAVE, idx=0),
+                I(ttc.OP_LOAD, idx=0), I(ttc.OP_SIGMOID), I(ttc.OP_MUL, ttc.SRC_SLOT, 0)]
+        d = ttc.chain_desc(N // 8, N, [ttc.in_view(x.data_ptr(), N, 1, N * N // 8)], [], prog,
+                           reduce=ttc.REDUCE_COLS, reduce_out=s.data_ptr(), nseg=8, reduce_seg_stride=N)
+    else:
+        progs = {
+            "copy": ([I(ttc.OP_LOAD, idx=0), I(ttc.OP_STORE, idx=0)], ttc.REDUCE_NONE),
+            "readme": ([I(ttc.OP_LOAD, idx=0), I(ttc.OP_RELU), I(ttc.OP_ADD, ttc.SRC_ACC), I(ttc.OP_MUL, ttc.SRC_ACC),
+                        I(ttc.OP_STORE, idx=0)], ttc.REDUCE_ALL),
+            "sigmoid": ([I(ttc.OP_LOAD, idx=0), I(ttc.OP_SIGMOID), I(ttc.OP_STORE, idx=0)], ttc.REDUCE_NONE),
+        }
+        prog, red = progs[name]
+        d = ttc.chain_desc(N, N, [ttc.in_view(x.data_ptr(), N)], [ttc.out_view(w.data_ptr(), N)], prog, reduce=red,
+                           reduce_out=s.data_ptr())
+    for _ in range(reps):
+        ttc.eltwise_chain(d)
+    torch.cuda.synchronize()
+    print(f"chain {name} {N}x{N} ok")
+
+
+def main(argv):
+    if len(argv) < 2 or argv[1] not in ("gemm", "chain"):
+        print(__doc__)
+        return 2
+    if argv[1] == "gemm":
+        gemm(int(argv[2]) if len(argv) > 2 else 8192)
+    else:
+        chain(argv[2] if len(argv) > 2 else "segments", int(argv[3]) if len(argv) > 3 else 8192)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main(sys.argv))
