@@ -74,9 +74,14 @@ class Clocks:
             import torch
 
             nv.nvmlInit()
-            p = torch.cuda.get_device_properties(self.device)
-            bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
-            self.h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            try:
+                p = torch.cuda.get_device_properties(self.device)
+                bus = f"{p.pci_domain_id:08x}:{p.pci_bus_id:02x}:{p.pci_device_id:02x}.0"
+                self.h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:  # noqa: BLE001 - no PCI ids: NVML index of the visible device
+                vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+                ids = [v for v in vis.split(",") if v.strip().isdigit()]
+                self.h = nv.nvmlDeviceGetHandleByIndex(int(ids[self.device]) if ids else self.device)
             self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
             self.nv = nv
             self.thread = threading.Thread(target=self._poll, daemon=True)
@@ -341,6 +346,19 @@ def run_ours(args):
     gemm_ms = g0.elapsed_time(g1) / reps
     gemm_tflops = 2 * Mg * N1 * K1 / (gemm_ms * 1e-3) / 1e12
     launches += reps + 3
+    # the opt-in CTA-pair kernel (tcgen05.mma.cta_group::2) on the same GEMM, for comparison
+    os.environ["TTC_GEMM_PAIR"] = "1"
+    for _ in range(3):
+        one_gemm()
+    torch.cuda.synchronize()
+    g0.record(stream)
+    for _ in range(reps):
+        one_gemm()
+    g1.record(stream)
+    torch.cuda.synchronize()
+    os.environ.pop("TTC_GEMM_PAIR")
+    pair_ms = g0.elapsed_time(g1) / reps
+    launches += reps + 3
     traffic = None
     tp = os.path.join(ROOT, "profiles", "tf32_gemm_traffic.txt")
     if os.path.exists(tp):
@@ -412,11 +430,13 @@ def run_ours(args):
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": int(X.nbytes), "d2h_bytes_per_step": int(K1 * 4),
                     "path": "tt_lazy Plan.run() over a streamed pinned-host X + to-host read of s"},
-            "roofline": {"bound": "tensor", "kernel": "tf32_gemm_kernel (tcgen05, 128x256 tiles)",
+            "roofline": {"bound": "tensor", "kernel": "tf32_gemm_kernel (tcgen05, 128x256 tile per CTA)",
                          "achieved": gemm_tflops, "peak": tf32_peak, "unit": "TFLOP/s",
                          "frac": gemm_tflops / tf32_peak, "traffic": traffic,
                          "peak_source": f"{peak_kind} bf16 dense / 2 (TF32 rate)",
-                         "launch_ms": gemm_ms, "shape": [Mg, N1, K1]},
+                         "launch_ms": gemm_ms, "shape": [Mg, N1, K1],
+                         "cta_pair_kernel": {"achieved": 2 * Mg * N1 * K1 / (pair_ms * 1e-3) / 1e12,
+                                             "launch_ms": pair_ms, "enabled_by": "TTC_GEMM_PAIR=1"}},
             "eltwise_chain": chain,
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),

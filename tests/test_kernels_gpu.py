@@ -296,7 +296,7 @@ def test_gemm_known_answer(ttc):
 
 
 @pytest.mark.parametrize("m,k,n", [(128, 32, 256), (256, 512, 1024), (256, 1024, 512), (384, 100, 300),
-                                   (1000, 260, 772), (128, 4096, 256)])
+                                   (1000, 260, 772), (128, 4096, 256), (520, 64, 1032), (1024, 512, 1280)])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
 def test_gemm_tf32(ttc, m, k, n, ta, tb):
     rng = np.random.default_rng(10)
@@ -304,6 +304,17 @@ def test_gemm_tf32(ttc, m, k, n, ta, tb):
     assert ttc.gemm_select_path(g) == ttc.GEMM_TF32
     err = normwise(got, want)
     assert err <= RTOL_TF32, err
+
+
+@pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (384, 100, 300), (1000, 260, 772), (520, 64, 1032),
+                                   (1024, 512, 1280)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_gemm_tf32_cta_pair(ttc, m, k, n, ta, tb, monkeypatch):
+    """The tcgen05.mma.cta_group::2 kernel (256x256 tile per CTA pair)."""
+    monkeypatch.setenv("TTC_GEMM_PAIR", "1")
+    rng = np.random.default_rng(13)
+    got, want, _ = _gemm_case(ttc, m, k, n, ta, tb, ttc.GEMM_TF32, rng, act="sigmoid", bias=True)
+    assert normwise(got, want) <= RTOL_TF32
 
 
 @pytest.mark.parametrize("path", ["ffma", "tf32"])

@@ -26,6 +26,7 @@
 // a multi-GPU run. Every mbarrier wait is bounded (about 2 s); an expired
 // wait records an error in a host-mapped status word, lets the other roles
 // time out too, waits for its own TMA loads, frees TMEM and returns.
+#include <cstdlib>
 #include <cstring>
 
 #include "tma_util.cuh"
@@ -296,6 +297,292 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                      : "memory");
 }
 
+// ------------------------------------------------------------------ pair MMA
+// The CTA-pair variant: a cluster of two CTAs on two SMs computes a 256x256
+// output tile with tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 8). CTA r of
+// the pair holds rows [128 r, 128 r + 128) of the A tile and columns
+// [128 r, 128 r + 128) of the B tile in its own shared memory, and receives
+// its 128 output rows x 256 columns in its own TMEM. Per 32-deep k-block a CTA
+// loads 32 KB (16 KB of A, 16 KB of B) instead of the single-CTA kernel's
+// 48 KB for the same 128x256 MACs: two thirds of the L2 -> SM traffic, which
+// is what bounds the single-CTA kernel.
+//
+// Roles (both CTAs): warp 0 TMA producer into this CTA's 6-stage ring, each
+// stage completing on this CTA's own full barrier; warp 1 of CTA 0 issues the
+// MMAs once both CTAs' stage is full, and commits stage / accumulator
+// releases to the barriers of both CTAs (one commit per CTA address); warp 1
+// of CTA 1 forwards "my stage s is full" to CTA 0 (it waits on its own full
+// barrier, so every CTA observes the completion of its own loads); warps 2-5
+// are the epilogue of the CTA's 128 rows and release the accumulator on
+// CTA 0's barrier (8 arrivals: 4 warps x 2 CTAs). All waits are bounded.
+// Every TMA load lands in the issuing CTA's own shared memory.
+constexpr int P_BNH = 128;                      // B columns per CTA
+constexpr int P_BN = 2 * P_BNH;                 // N of the pair tile
+constexpr int P_STAGES = 6;
+constexpr int P_A_BYTES = BM * BK * 4;          // 16 KB
+constexpr int P_B_BYTES = P_BNH * BK * 4;       // 16 KB
+constexpr int P_STAGE_BYTES = P_A_BYTES + P_B_BYTES;
+constexpr int P_TMEM_COLS = 2 * P_BN;           // two 128 x 256 accumulators
+constexpr int P_GROUP_M = 8;                    // pair-tile rows per raster group
+constexpr int P_SMEM_BYTES = P_STAGES * P_STAGE_BYTES + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// Address of the same shared-memory offset in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+    uint32_t out;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(local), "r"(rank));
+    return out;
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// Relaxed remote arrive for the per-stage forward: the forwarding thread has
+// already observed the stage's TMA bytes land (its own full barrier), so the
+// data is in shared memory before the arrive; a release arrive would add a
+// cluster-scope fence to every k-block and made the forward the bottleneck
+// (about 1.5k cycles each, measured: 358 vs 827 TFLOP/s on zero data).
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tc2_commit(uint32_t cluster_bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc2_mma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+__device__ __forceinline__ void pair_tile_coords(int tile, int m2_blocks, int n_blocks, int& mb2, int& nb) {
+    const int per_group = P_GROUP_M * n_blocks;
+    const int group = tile / per_group;
+    const int first_m = group * P_GROUP_M;
+    const int gm = min(P_GROUP_M, m2_blocks - first_m);
+    const int local = tile - group * per_group;
+    mb2 = first_m + local % gm;
+    nb = local / gm;
+}
+
+// p.m_blocks counts 256-row pair tiles, p.n_blocks 256-column tiles.
+__global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __grid_constant__ TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t* bars = (uint64_t*)(smem + P_STAGES * P_STAGE_BYTES);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * P_STAGES + 4);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_rank();
+    const uint32_t sbase = smem_u32(smem);
+    const uint32_t bar0 = smem_u32(bars);
+    auto full_bar = [&](int s) { return bar0 + 8u * s; };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (P_STAGES + s); };
+    auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * P_STAGES + b); };
+    auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * P_STAGES + 2 + b); };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < P_STAGES; ++s) {
+            mbar_init(full_bar(s), rank == 0 ? 2 : 1);  // CTA 0: own producer + the peer's forward
+            mbar_init(empty_bar(s), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(tfull_bar(b), 1);
+            mbar_init(tempty_bar(b), 8);
+        }
+        mbar_fence_init();
+    }
+    if (p.epi.has_sigmoid) exp2_table_init_block();
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(P_TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // both CTAs' barriers are initialised before anyone signals across
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+    const int num_tiles = p.m_blocks * p.n_blocks;
+    const int cluster_id = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+    bool failed = false;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tensor_map(&p.tma_a);
+            prefetch_tensor_map(&p.tma_b);
+            int stage = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            for (int tile = cluster_id; tile < num_tiles && !failed; tile += nclusters) {
+                int mb2, nb;
+                pair_tile_coords(tile, p.m_blocks, p.n_blocks, mb2, nb);
+                const int row0 = mb2 * (2 * BM) + (int)rank * BM;
+                const int col0 = nb * P_BN + (int)rank * P_BNH;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1)) {
+                        failed = true;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(full_bar(stage), P_STAGE_BYTES);
+                    const uint32_t a_dst = sbase + stage * P_STAGE_BYTES, b_dst = a_dst + P_A_BYTES;
+                    if (!p.a_mn_major) {
+                        tma_load_2d(a_dst, &p.tma_a, full_bar(stage), kb * BK, row0);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BM / 32; ++j)
+                            tma_load_2d(a_dst + j * (BK * 128), &p.tma_a, full_bar(stage), row0 + 32 * j, kb * BK);
+                    }
+                    if (!p.b_mn_major) {
+                        tma_load_2d(b_dst, &p.tma_b, full_bar(stage), kb * BK, col0);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < P_BNH / 32; ++j)
+                            tma_load_2d(b_dst + j * (BK * 128), &p.tma_b, full_bar(stage), col0 + 32 * j, kb * BK);
+                    }
+                    ++issued;
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+            // Never leave with loads in flight (CTA 1's own full barrier sees
+            // exactly its loads; CTA 0's also needs the peer's forward, which
+            // comes unless the peer failed -- then this wait expires).
+            const long long last = issued < P_STAGES ? issued : P_STAGES;
+            for (long long i = 0; i < last; ++i) {
+                const long long n = issued - 1 - i;
+                if (!mbar_wait(full_bar((int)(n % P_STAGES)), (uint32_t)((n / P_STAGES) & 1))) failed = true;
+            }
+        }
+    } else if (warp == 1 && rank == 1) {
+        if (lane == 0) {
+            // forward every completed stage of this CTA to CTA 0's full barrier
+            int stage = 0;
+            uint32_t phase = 0;
+            for (int tile = cluster_id; tile < num_tiles && !failed; tile += nclusters) {
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase)) {
+                        failed = true;
+                        break;
+                    }
+                    mbar_arrive_cluster_relaxed(cluster_addr(full_bar(stage), 0));
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t a_lbo = p.a_mn_major ? BK * 128 : 16, a_sbo = p.a_mn_major ? 512 : 1024;
+            const uint32_t b_lbo = p.b_mn_major ? BK * 128 : 16, b_sbo = p.b_mn_major ? 512 : 1024;
+            const uint32_t a_lay = p.a_mn_major ? kLayoutSW128Base32 : kLayoutSW128;
+            const uint32_t b_lay = p.b_mn_major ? kLayoutSW128Base32 : kLayoutSW128;
+            const uint32_t a_kstep = p.a_mn_major ? 8 * 128 : 32;
+            const uint32_t b_kstep = p.b_mn_major ? 8 * 128 : 32;
+            int stage = 0;
+            uint32_t phase = 0;
+            int t = 0;
+            for (int tile = cluster_id; tile < num_tiles && !failed; tile += nclusters, ++t) {
+                const int b = t & 1;
+                const uint32_t acc_phase = (t >> 1) & 1;
+                if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + (uint32_t)(b * P_BN);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    if (!mbar_wait(full_bar(stage), phase)) {
+                        failed = true;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_s = sbase + stage * P_STAGE_BYTES, b_s = a_s + P_A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 8; ++k) {
+                        const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, a_sbo, a_lay);
+                        const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, b_sbo, b_lay);
+                        tc2_mma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                    }
+                    tc2_commit(cluster_addr(empty_bar(stage), 0));
+                    tc2_commit(cluster_addr(empty_bar(stage), 1));
+                    if (++stage == P_STAGES) {
+                        stage = 0;
+                        phase ^= 1;
+                    }
+                }
+                if (failed) break;
+                tc2_commit(cluster_addr(tfull_bar(b), 0));
+                tc2_commit(cluster_addr(tfull_bar(b), 1));
+            }
+        }
+    } else {
+        const int q = warp & 3;  // this warp's quarter of the 128 TMEM lanes
+        int t = 0;
+        for (int tile = cluster_id; tile < num_tiles; tile += nclusters, ++t) {
+            int mb2, nb;
+            pair_tile_coords(tile, p.m_blocks, p.n_blocks, mb2, nb);
+            const int b = t & 1;
+            const uint32_t acc_phase = (t >> 1) & 1;
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase));
+            if (!ok) {
+                failed = true;
+                break;
+            }
+            tc_fence_after();
+            const long long row = (long long)mb2 * (2 * BM) + rank * BM + q * 32 + lane;
+            for (int c = 0; c < P_BN / 32; ++c) {
+                uint32_t r[32];
+                tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * P_BN + c * 32), r);
+                tc_wait_ld();
+                const long long col0 = (long long)nb * P_BN + c * 32;
+                if (col0 >= p.N) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    float v[4][4];
+                    long long rr[4], cc[4];
+                    bool vv[4];
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        rr[g] = row;
+                        cc[g] = col0 + h * 16 + g * 4;
+                        vv[g] = row < p.M && cc[g] < p.N;
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) v[g][w] = __uint_as_float(r[h * 16 + g * 4 + w]);
+                    }
+                    run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(cluster_addr(tempty_bar(b), 0));
+        }
+    }
+
+    if (failed) *(volatile int*)p.status = 1;
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();  // the pair's MMAs and signals are done before TMEM is freed or a CTA exits
+    tc_fence_after();
+    if (warp == 1)
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(P_TMEM_COLS)
+                     : "memory");
+}
+
 // 2-D fp32 tensor map over a row-major matrix with `outer` rows of `inner`
 // elements (row pitch ld elements), box {32, box_outer}, out-of-bounds reads
 // filled with zeros. K-major tiles use the 16-byte-chunk 128-byte swizzle;
@@ -321,12 +608,62 @@ bool tf32_supported(const ttc_gemm_desc& d, const DProgram& epi, bool epi_vec) {
     return true;
 }
 
+namespace {
+
+// The CTA-pair kernel runs when TTC_GEMM_PAIR=1 (read at every call) and the
+// GEMM has at least one 256x256 tile. It is not the default: alone (burst
+// clocks) it is up to ~10% faster than the single-CTA kernel, but inside the
+// long power-capped MLP step both are held to the 1 kW limit and the pair
+// kernel's SM clock drops further (measured back to back: 496-499 vs 507-517
+// TFLOP/s per step, 1.07-1.09 vs 1.28-1.31 GHz), so the step is ~3% slower.
+bool use_pair(const ttc_gemm_desc& d) {
+    const char* e = getenv("TTC_GEMM_PAIR");
+    return e && e[0] == '1' && d.M >= 2 * BM && d.N >= P_BN;
+}
+
+int launch_pair(TcParams& p) {
+    static int max_clusters = -1;
+    cudaLaunchConfig_t cfg;
+    std::memset(&cfg, 0, sizeof cfg);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads, 1, 1);
+    cfg.dynamicSmemBytes = P_SMEM_BYTES;
+    cfg.stream = rt().stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (max_clusters < 0) {
+        TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      P_SMEM_BYTES));
+        cfg.gridDim = dim3(2 * (rt().sm_count / 2), 1, 1);
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, tf32_gemm_pair_kernel, &cfg) != cudaSuccess || n < 1) {
+            cudaGetLastError();
+            n = rt().sm_count / 2;
+        }
+        max_clusters = n;
+    }
+    const long long tiles = (long long)p.m_blocks * p.n_blocks;
+    const int clusters = (int)(tiles < max_clusters ? tiles : max_clusters);
+    cfg.gridDim = dim3(2 * clusters, 1, 1);
+    TTC_CUDA(cudaLaunchKernelEx(&cfg, tf32_gemm_pair_kernel, p));
+    count_launch();
+    return TTC_OK;
+}
+
+}  // namespace
+
 int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi) {
     static bool attr_set = false;
     if (!attr_set) {
         TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         attr_set = true;
     }
+    const bool pair = use_pair(d);
+    const int bn = pair ? P_BNH : BN;  // B columns one CTA loads per tile
     TcParams p;
     std::memset(&p, 0, sizeof p);
     p.a_mn_major = d.trans_a ? 1 : 0;
@@ -341,23 +678,28 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi) {
     if (p.b_mn_major) {
         if (int rc = make_map(&p.tma_b, d.b, d.N, d.K, d.ldb, BK, true)) return rc;
     } else {
-        if (int rc = make_map(&p.tma_b, d.b, d.K, d.N, d.ldb, BN, false)) return rc;
+        if (int rc = make_map(&p.tma_b, d.b, d.K, d.N, d.ldb, bn, false)) return rc;
     }
     p.M = d.M;
     p.N = d.N;
     p.K = d.K;
-    p.m_blocks = (d.M + BM - 1) / BM;
-    p.n_blocks = (d.N + BN - 1) / BN;
+    const int tm = pair ? 2 * BM : BM, tn = pair ? P_BN : BN;  // output tile of one CTA / CTA pair
+    p.m_blocks = (d.M + tm - 1) / tm;
+    p.n_blocks = (d.N + tn - 1) / tn;
     p.k_blocks = (d.K + BK - 1) / BK;
     p.idesc = (1u << 4)                       // D format: f32
               | (2u << 7) | (2u << 10)        // A, B format: tf32
               | ((unsigned)p.a_mn_major << 15) | ((unsigned)p.b_mn_major << 16) |
-              ((unsigned)(BN >> 3) << 17)     // N
-              | ((unsigned)(BM >> 4) << 24);  // M
+              ((unsigned)(tn >> 3) << 17)     // N
+              | ((unsigned)(tm >> 4) << 24);  // M (256 for the pair: 128 rows per CTA)
     if (int rc = device_status_ptr(&p.status)) return rc;
     p.epi = epi;
     const long long tiles = (long long)p.m_blocks * p.n_blocks;
     if (tiles > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many GEMM tiles");
+    if (pair) {
+        if (int rc = launch_pair(p)) return rc;
+        return check_cuda(cudaGetLastError(), "TF32 pair GEMM launch");
+    }
     const int grid = (int)(tiles < rt().sm_count ? tiles : rt().sm_count);
     tf32_gemm_kernel<<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
     count_launch();
