@@ -8,7 +8,7 @@
  * C++ (`Tensor math::relu(const Tensor&)`, errors thrown as
  * std::runtime_error); this seam is plain C: device pointers, sizes and
  * strides in, an int status out, no C++ exception ever crosses it. The C++
- * operation handlers (tt_lazy_b200/host/OperationHandlers.cpp) turn a non-zero
+ * operation handlers (tt_lazy_b200/host/Executor.cpp) turn a non-zero
  * status back into std::runtime_error(ttc_last_error()), which keeps the
  * reference's error behaviour for tt_lazy users.
  *
@@ -72,6 +72,15 @@ int ttc_memcpy_h2d(void* dst, const void* src, size_t bytes);
 /* device -> host, synchronous: the single materialisation copy that stands in
  * for the memcpy of Tensor::eval_impl (src/core/Tensor.cpp:572). */
 int ttc_memcpy_d2h(void* dst, const void* src, size_t bytes);
+/* Host -> device prefetch on the library's copy stream (no reference
+ * counterpart: it lets the upload of one batch chunk overlap the kernels of
+ * the previous one). The copy starts after all work already enqueued on the
+ * library stream; *ticket names it for ttc_wait_ticket, which makes later
+ * work on the library stream wait for the copy. src should be pinned
+ * (ttc_host_alloc) for the copy to run asynchronously. Up to 256 prefetches
+ * may be outstanding. */
+int ttc_h2d_prefetch(void* dst, const void* src, size_t bytes, int* ticket);
+int ttc_wait_ticket(int ticket);
 int ttc_memcpy_d2d(void* dst, const void* src, size_t bytes);
 int ttc_memset_zero(void* dst, size_t bytes);
 /* Pinned host memory for staging (cudaHostAlloc). */
@@ -105,8 +114,10 @@ int ttc_get_memory_stats(ttc_memory_stats* out);
  *   SAVE s       slot[s] = acc
  *   STORE k      output[k] = acc
  * Every step is one IEEE single operation (no FMA contraction), so results
- * are bit-identical to the reference's separate passes; SIGMOID uses CUDA's
- * expf and IEEE division (within 2 ulp of the CPU value).
+ * are bit-identical to the reference's separate passes; SIGMOID rounds a
+ * table-driven e^-x (relative error below 2^-44) once, then adds and takes
+ * the IEEE reciprocal, so it equals the CPU's 1/(1+expf(-x)) on nearly every
+ * input and stays within 2 ulp of it everywhere.
  *
  * Views: element (r, c) of segment g of input k is
  *   ptr[g*seg_stride + r*row_stride + c*col_stride]

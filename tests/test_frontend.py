@@ -144,3 +144,33 @@ def test_random_dag_fusion_is_acyclic_and_complete():
             assert i in produced, "operation reads a result produced later"
         produced.update(op["outputs"])
         produced.add(op["node"])
+
+
+def test_pipelined_plan_rebuilds_the_graph_over_row_chunks():
+    X = np.random.default_rng(0).standard_normal((64, 16)).astype(np.float32)
+    xs = tl.streamed(X)
+    W1, W2 = c((16, 32), 1), c((32, 8), 2)
+    s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xs, W1)), W2)), [0])
+    assert ops([s]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid]", "Reduce"]
+    assert len(tl.Plan([s])) == 3
+    # 4 chunks x (GEMM, GEMM, partial sum) + the chunk-order sum of the partials (one fused chain)
+    assert len(tl.Plan([s], pipeline_chunks=4)) == 13
+    # the all-reduce runs once, after the partial sums are combined
+    assert len(tl.Plan([tl.all_reduce_sum(s)], pipeline_chunks=3)) == 11
+
+
+def test_pipelined_plan_rejects_graphs_that_are_not_row_local():
+    X = np.random.default_rng(0).standard_normal((64, 16)).astype(np.float32)
+    xs = tl.streamed(X)
+    bad = {
+        "Transpose is not row-local": tl.reduce_sum(tl.transpose(xs), [0]),
+        "every output must be reduce_sum": tl.relu(xs),
+        "not row-chunked": tl.reduce_sum(tl.add(xs, c((64, 16), 3)), [0]),
+    }
+    for msg, out in bad.items():
+        with pytest.raises(RuntimeError, match=msg):
+            tl.Plan([out], pipeline_chunks=2)
+    with pytest.raises(RuntimeError, match="streamed rank-2 batch input"):
+        tl.Plan([tl.reduce_sum(tl.relu(c((8, 8))), [0])], pipeline_chunks=2)
+    with pytest.raises(RuntimeError, match="chunks must be"):
+        tl.Plan([tl.reduce_sum(tl.relu(xs), [0])], pipeline_chunks=65)

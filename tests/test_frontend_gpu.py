@@ -263,3 +263,29 @@ def test_random_dag_matches_oracle():
         want = oracle.reduce(host[s], (1,), f64=True)
         scale = np.abs(host[s]).astype(np.float64).sum(axis=1) + 1e-30
         assert np.all(np.abs(o.numpy() - want) <= 1e-4 * scale)
+
+
+@pytest.mark.parametrize("chunks", [2, 5])
+def test_pipelined_plan_matches_the_whole_batch_plan(chunks):
+    """Row chunks of a streamed batch, uploaded on the copy stream while
+    earlier chunks compute, give the same column sums as one whole-batch
+    evaluation (up to the order of the partial sums) and as the oracle."""
+    tl.set_gemm_path("ffma")
+    rng = np.random.default_rng(31)
+    X = rng.standard_normal((1000, 128)).astype(np.float32)
+    W1 = (rng.standard_normal((128, 256)) / np.sqrt(128)).astype(np.float32)
+    W2 = (rng.standard_normal((256, 64)) / 16).astype(np.float32)
+    xs = tl.streamed(X)
+    s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xs, tl.constant(W1))), tl.constant(W2))), [0])
+    whole, piped = tl.Plan([s]), tl.Plan([s], pipeline_chunks=chunks)
+    whole.run()
+    for _ in range(2):  # runs reuse the plan (and its device buffers)
+        piped.run()
+        got = piped.numpy(0)
+        assert np.allclose(got, whole.numpy(0), rtol=1e-5, atol=1e-5)
+    want = oracle.reduce(oracle.sigmoid(oracle.matmul(oracle.relu(oracle.matmul(X, W1)), W2)), (0,), f64=True)
+    assert np.allclose(got, want, rtol=1e-5, atol=1e-5)
+    X[:] = rng.standard_normal(X.shape).astype(np.float32)  # a new batch in the same host buffer
+    piped.run()
+    want = oracle.reduce(oracle.sigmoid(oracle.matmul(oracle.relu(oracle.matmul(X, W1)), W2)), (0,), f64=True)
+    assert np.allclose(piped.numpy(0), want, rtol=1e-5, atol=1e-5)

@@ -292,6 +292,13 @@ int ttc_shutdown(void) {
     Runtime& r = rt();
     if (!r.initialized) return TTC_OK;
     cudaStreamSynchronize(r.stream);
+    if (r.copy_stream) {
+        cudaStreamSynchronize(r.copy_stream);
+        for (auto& e : r.tickets)
+            if (e) cudaEventDestroy(e), e = nullptr;
+        cudaStreamDestroy(r.copy_stream);
+        r.copy_stream = nullptr;
+    }
     if (r.workspace) cudaFree(r.workspace);
     r.workspace = nullptr;
     r.workspace_bytes = 0;
@@ -352,6 +359,37 @@ int ttc_memcpy_h2d(void* dst, const void* src, size_t bytes) {
     TTC_REQUIRE_INIT();
     if (bytes == 0) return TTC_OK;
     TTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, rt().stream));
+    return TTC_OK;
+}
+
+// Copies on a second stream so that they overlap kernels on the library
+// stream. The copy stream first waits for everything already enqueued on the
+// library stream, so a prefetch never overwrites a buffer that earlier
+// kernels still read; ttc_wait_ticket then orders later kernels after it.
+int ttc_h2d_prefetch(void* dst, const void* src, size_t bytes, int* ticket) {
+    TTC_REQUIRE_INIT();
+    if (!ticket || (!dst && bytes) || (!src && bytes))
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: h2d_prefetch: null argument");
+    Runtime& r = rt();
+    if (!r.copy_stream) {
+        TTC_CUDA(cudaStreamCreateWithFlags(&r.copy_stream, cudaStreamNonBlocking));
+        for (auto& e : r.tickets) TTC_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    }
+    const unsigned t = r.next_ticket++ % 256u;
+    TTC_CUDA(cudaEventRecord(r.tickets[t], r.stream));
+    TTC_CUDA(cudaStreamWaitEvent(r.copy_stream, r.tickets[t], 0));
+    if (bytes) TTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, r.copy_stream));
+    TTC_CUDA(cudaEventRecord(r.tickets[t], r.copy_stream));
+    *ticket = (int)t;
+    return TTC_OK;
+}
+
+int ttc_wait_ticket(int ticket) {
+    TTC_REQUIRE_INIT();
+    Runtime& r = rt();
+    if (ticket < 0 || ticket >= 256 || !r.copy_stream)
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: wait_ticket: no prefetch %d", ticket);
+    TTC_CUDA(cudaStreamWaitEvent(r.stream, r.tickets[ticket], 0));
     return TTC_OK;
 }
 

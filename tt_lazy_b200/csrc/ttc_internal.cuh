@@ -30,6 +30,9 @@ struct Runtime {
     size_t workspace_bytes = 0;
     size_t bytes_in_use = 0, peak_bytes = 0;
     unsigned long long kernels = 0;
+    cudaStream_t copy_stream = nullptr;  // host-to-device prefetch (ttc_h2d_prefetch)
+    cudaEvent_t tickets[256] = {};       // completion events of prefetches, a ring
+    unsigned next_ticket = 0;
 };
 Runtime& rt();
 // Scratch of at least `bytes`, valid until the next call that asks for more.

@@ -137,11 +137,25 @@ void set_contiguous_strides(DeviceView& v, const std::vector<uint32_t>& shape) {
 }
 }  // namespace
 
+// Streamed inputs whose upload a pipelined plan started on the copy stream:
+// (host pointer, elements) -> (device view, prefetch ticket).
+std::map<std::pair<const void*, size_t>, std::pair<DeviceView, int>>& prefetched() {
+    static auto* m = new std::map<std::pair<const void*, size_t>, std::pair<DeviceView, int>>();
+    return *m;
+}
+
 DeviceView upload(const Tensor& t) {
     if (t.has_device()) return t.device();
     const float* host = t.host_data();
     if (!host) throw std::runtime_error("tt_lazy: input tensor has no data");
     const size_t n = t.total_elements();
+    if (t.is_streamed()) {
+        auto it = prefetched().find(std::make_pair((const void*)host, n));
+        if (it != prefetched().end()) {  // kernels from here on wait for that copy
+            check(ttc_wait_ticket(it->second.second));
+            return it->second.first;
+        }
+    }
     const bool cached = t.is_constant() && !t.is_streamed();
     if (cached) {
         auto key = std::make_pair((const void*)host, n);
@@ -1068,12 +1082,25 @@ EvaluationManager& get_evaluation_manager() {
     return *instance;
 }
 
-CompiledTape::CompiledTape(const std::vector<Tensor>& outputs) : outputs_(outputs) {
+CompiledTape::CompiledTape(const std::vector<Tensor>& outputs, int pipeline_chunks) : outputs_(outputs) {
     for (const auto& t : outputs)
         if (!t.is_lazy()) throw std::runtime_error("CompiledTape: outputs must be lazy tensors");
+    if (pipeline_chunks > 1) outputs_ = build_row_pipeline(outputs, pipeline_chunks);
     TapeGenerator gen;
-    tape_ = gen.generate_tape(outputs);
+    tape_ = gen.generate_tape(outputs_);
     register_all_operations(executor_);
+    if (pipeline_chunks > 1) {
+        // the row chunks of the streamed batch, in the order the tape reads them
+        std::set<std::pair<const void*, size_t>> seen;
+        for (const auto& op : tape_->operations()) {
+            std::vector<OperandRef> refs = op->operands;
+            if (op->plan) refs.insert(refs.end(), op->plan->externals.begin(), op->plan->externals.end());
+            for (const auto& o : refs)
+                if (!o.lazy && o.tensor.is_streamed() &&
+                    seen.insert({(const void*)o.tensor.host_data(), o.tensor.total_elements()}).second)
+                    prefetch_.push_back(o.tensor);
+        }
+    }
 }
 
 void CompiledTape::run() {
@@ -1083,6 +1110,19 @@ void CompiledTape::run() {
     for (const auto& op : tape_->operations()) op->is_evaluated = false;
     results_.clear();
     executor_.clear_results();
+    // start every chunk's upload on the copy stream; chunk c's kernels wait for chunk c only
+    for (const auto& t : prefetch_) {
+        DeviceView v;
+        const size_t n = t.total_elements();
+        v.buf = MemoryManager::instance().allocate(n * sizeof(float));
+        set_contiguous_strides(v, t.shape_vector());
+        int ticket = -1;
+        check(ttc_h2d_prefetch(v.buf->ptr(), t.host_data(), n * sizeof(float), &ticket));
+        prefetched()[{(const void*)t.host_data(), n}] = {v, ticket};
+    }
+    struct Clear {
+        ~Clear() { prefetched().clear(); }
+    } clear_prefetched;
     executor_.execute_tape(*tape_);
     for (const auto& t : outputs_) {
         auto r = executor_.get_result(t.producer_node(), t.output_index());

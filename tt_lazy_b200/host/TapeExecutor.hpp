@@ -162,9 +162,12 @@ void evaluate(std::vector<Tensor*> tensors);
 // loop of a fixed graph. Constant inputs stay resident on the device,
 // streamed inputs are re-uploaded on every run(), results stay on the
 // device until fetched.
+// pipeline_chunks > 1: the graph is rebuilt over that many row chunks of its
+// streamed batch input (build_row_pipeline) and each chunk's upload overlaps
+// the kernels of the chunks before it.
 class CompiledTape {
    public:
-    explicit CompiledTape(const std::vector<Tensor>& outputs);
+    explicit CompiledTape(const std::vector<Tensor>& outputs, int pipeline_chunks = 1);
     void run();
     std::shared_ptr<Tensor> result(size_t i) const;
     size_t size() const { return tape_->size(); }
@@ -176,8 +179,14 @@ class CompiledTape {
     std::unique_ptr<Tape> tape_;
     TapeExecutor executor_;
     std::vector<std::shared_ptr<Tensor>> results_;
+    std::vector<Tensor> prefetch_;  // streamed chunk inputs uploaded on the copy stream
     size_t kernels_ = 0;
 };
+
+// Row-chunked form of `outputs` over their one streamed rank-2 batch input
+// (Pipeline.cpp); throws std::runtime_error when the graph is not row-local
+// up to a batch-dim reduce_sum (optionally followed by all_reduce_sum).
+std::vector<Tensor> build_row_pipeline(const std::vector<Tensor>& outputs, int chunks);
 
 // Data parallelism across processes (one per GPU): an NCCL communicator and
 // the all-reduce op of the front end (operations.hpp: all_reduce_sum).

@@ -102,7 +102,7 @@ PYBIND11_MODULE(_tt_lazy, m) {
     m.def("comm_destroy", &tt_lazy::comm_destroy);
 
     py::class_<tt_lazy::CompiledTape>(m, "Plan")
-        .def(py::init<const std::vector<Tensor>&>())
+        .def(py::init<const std::vector<Tensor>&, int>(), py::arg("outputs"), py::arg("pipeline_chunks") = 1)
         .def("run", &tt_lazy::CompiledTape::run, py::call_guard<py::gil_scoped_release>())
         .def("numpy",
              [](const tt_lazy::CompiledTape& p, size_t i) {
