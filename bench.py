@@ -304,7 +304,7 @@ def run_ours(args):
     Xp[...] = X
     s_e2e = graph(tl.streamed(Xp))
     # row-chunked plan: chunk c + 1 uploads on the copy stream while chunk c computes
-    chunks = max(1, min(8, rows // 4096))
+    chunks = max(1, min(8, rows // 2048))
     plan_e2e = tl.Plan([s_e2e], pipeline_chunks=chunks) if chunks > 1 else tl.Plan([s_e2e])
     for _ in range(max(1, args.warmup - 1)):
         plan_e2e.run()

@@ -289,3 +289,49 @@ def test_pipelined_plan_matches_the_whole_batch_plan(chunks):
     piped.run()
     want = oracle.reduce(oracle.sigmoid(oracle.matmul(oracle.relu(oracle.matmul(X, W1)), W2)), (0,), f64=True)
     assert np.allclose(piped.numpy(0), want, rtol=1e-5, atol=1e-5)
+
+
+def test_large_mlp_at_full_size_on_sampled_rows():
+    """The 65536 x 4096 -> 16384 -> 4096 MLP at its full size (TF32 tensor-core
+    GEMMs, fused relu / sigmoid epilogues, batch column sums): sampled rows of
+    Y against the oracle (rows are independent), s against the fp64 sum of the
+    GPU's own Y, and the row-pipelined plan against the whole-batch plan."""
+    rng = np.random.default_rng(2)
+    M, K, N = 65536, 4096, 16384
+    X = rng.standard_normal((M, K), dtype=np.float32)
+    W1 = (rng.standard_normal((K, N), dtype=np.float32) / np.float32(np.sqrt(K)))
+    W2 = (rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(N)))
+    xs = tl.streamed(X)
+    y = tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xs, tl.constant(W1))), tl.constant(W2)))
+    s = tl.reduce_sum(y, [0])
+    tl.evaluate([y, s])
+    Y, S = y.numpy(), s.numpy()
+    rows = [0, 1, 4095, 4096, 32767, 40000, 65534, 65535]
+    want = oracle.sigmoid(oracle.matmul(oracle.relu(oracle.matmul(X[rows], W1)), W2))
+    assert normwise(Y[rows], want) <= 2e-3
+    exact = Y.astype(np.float64).sum(axis=0)
+    assert np.max(np.abs(S - exact) / np.abs(exact)) <= 1e-5
+    s2 = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xs, tl.constant(W1))), tl.constant(W2))), [0])
+    piped = tl.Plan([s2], pipeline_chunks=8)  # s itself is materialised by now
+    piped.run()
+    assert np.allclose(piped.numpy(0), S, rtol=1e-5, atol=0)
+
+
+def test_bandwidth_graph_at_full_size_on_sampled_outputs():
+    """A[16384, 16384]: transpose -> 8 column chunks -> sigmoid(C) * relu(C + C)
+    -> row sums, one segmented launch; sampled outputs of every chunk against
+    the fp64 sum of the oracle's element-wise values."""
+    rng = np.random.default_rng(3)
+    n, w = 16384, 2048
+    A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+    outs = [tl.reduce_sum(tl.multiply(tl.sigmoid(ch), tl.relu(tl.add(ch, ch))), [1])
+            for ch in tl.split(tl.transpose(tl.constant(A)), w, 1)]
+    tl.evaluate(outs)
+    for i, o in enumerate(outs):
+        got = o.numpy()
+        assert got.shape == (n,)
+        for j in (0, 1, 777, 8191, 16383):
+            c = np.ascontiguousarray(A[w * i:w * (i + 1), j])  # row j of chunk i of the transpose
+            y = oracle.multiply(oracle.sigmoid(c), oracle.relu(oracle.add(c, c)))
+            exact = y.astype(np.float64).sum()
+            assert abs(got[j] - exact) <= 1e-5 * max(abs(exact), 1e-30), (i, j, got[j], exact)
