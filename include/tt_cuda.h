@@ -81,6 +81,16 @@ int ttc_memcpy_d2h(void* dst, const void* src, size_t bytes);
  * may be outstanding. */
 int ttc_h2d_prefetch(void* dst, const void* src, size_t bytes, int* ticket);
 int ttc_wait_ticket(int ticket);
+/* CUDA-graph capture of the library stream (no reference counterpart: a
+ * compiled tape replayed with one launch instead of one per kernel). Between
+ * ttc_capture_begin and ttc_capture_end the library's calls are recorded,
+ * not run; they must not synchronise with the host (no ttc_memcpy_d2h, no
+ * all-reduce). ttc_capture_end instantiates the recording into an opaque
+ * executable graph, ttc_graph_launch replays it on the library stream. */
+int ttc_capture_begin(void);
+int ttc_capture_end(void** graph_exec);
+int ttc_graph_launch(void* graph_exec);
+int ttc_graph_destroy(void* graph_exec);
 int ttc_memcpy_d2d(void* dst, const void* src, size_t bytes);
 int ttc_memset_zero(void* dst, size_t bytes);
 /* Pinned host memory for staging (cudaHostAlloc). */

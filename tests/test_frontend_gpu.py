@@ -335,3 +335,71 @@ def test_bandwidth_graph_at_full_size_on_sampled_outputs():
             y = oracle.multiply(oracle.sigmoid(c), oracle.relu(oracle.add(c, c)))
             exact = y.astype(np.float64).sum()
             assert abs(got[j] - exact) <= 1e-5 * max(abs(exact), 1e-30), (i, j, got[j], exact)
+
+
+def test_empty_and_degenerate_shapes():
+    """Empty batches, an empty contraction and a split larger than its dim,
+    as the reference's math functions handle them (empty results; a sum over
+    nothing is 0; one chunk)."""
+    e = np.zeros((0, 8), np.float32)
+    assert tl.relu(tl.constant(e)).numpy().shape == (0, 8)
+    assert tl.add(tl.constant(e), tl.constant(e)).numpy().shape == (0, 8)
+    assert tl.sigmoid(tl.constant(e)).numpy().shape == (0, 8)
+    assert np.array_equal(tl.reduce_sum(tl.constant(e), [0]).numpy(), np.zeros(8, np.float32))
+    assert tl.reduce_sum(tl.constant(e), [1]).numpy().shape == (0,)
+    for path in ("ffma", "tf32"):
+        tl.set_gemm_path(path)
+        a = np.ones((0, 16), np.float32)
+        assert tl.matmul(tl.constant(a), tl.constant(np.ones((16, 8), np.float32))).numpy().shape == (0, 8)
+        z = tl.matmul(tl.constant(np.ones((4, 0), np.float32)), tl.constant(np.ones((0, 8), np.float32))).numpy()
+        assert z.shape == (4, 8) and np.all(z == 0)
+    x = np.arange(15, dtype=np.float32).reshape(5, 3)
+    parts = tl.split(tl.constant(x), 10, 0)
+    assert len(parts) == 1 and np.array_equal(parts[0].numpy(), x)
+
+
+def test_captured_plan_replays_the_tape_as_one_graph():
+    """Plan.capture(): one warm run, then the tape recorded into a CUDA graph;
+    replays give the same bits as the uncaptured plan, and a streamed input
+    is re-read from its host memory on every replay."""
+    rng = np.random.default_rng(41)
+    x = rng.uniform(-1, 1, (1000, 1000)).astype(np.float32)
+    xs = tl.streamed(x)
+    y = tl.relu(xs)
+    z = tl.add(y, y)
+    w = tl.multiply(z, z)
+    s = tl.reduce_sum(w)
+    plain, cap = tl.Plan([w, s]), tl.Plan([w, s])
+    plain.run()
+    cap.capture()
+    assert cap.captured
+    for _ in range(3):
+        cap.run()
+        assert np.array_equal(cap.numpy(0), plain.numpy(0))
+        assert np.array_equal(cap.numpy(1), plain.numpy(1))
+    x[:] = rng.uniform(-1, 1, x.shape).astype(np.float32)
+    cap.run()
+    ow = oracle.multiply(oracle.add(oracle.relu(x), oracle.relu(x)), oracle.add(oracle.relu(x), oracle.relu(x)))
+    assert np.array_equal(cap.numpy(0), ow)
+    exact = oracle.reduce(ow, f64=True)[0]
+    assert abs(cap.numpy(1)[0] - exact) <= 1e-5 * abs(exact)
+
+
+def test_captured_pipelined_mlp_plan():
+    tl.set_gemm_path("tf32")
+    rng = np.random.default_rng(42)
+    X = rng.standard_normal((2048, 256)).astype(np.float32)
+    W1 = (rng.standard_normal((256, 512)) / 16).astype(np.float32)
+    W2 = (rng.standard_normal((512, 256)) / np.sqrt(512)).astype(np.float32)
+    xs = tl.streamed(X)
+    s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xs, tl.constant(W1))), tl.constant(W2))), [0])
+    plain, cap = tl.Plan([s], pipeline_chunks=4), tl.Plan([s], pipeline_chunks=4)
+    plain.run()
+    cap.capture()
+    for _ in range(2):
+        cap.run()
+        assert np.array_equal(cap.numpy(0), plain.numpy(0))
+    want = oracle.reduce(oracle.sigmoid(oracle.matmul(oracle.relu(oracle.matmul(X, W1)), W2)), (0,), f64=True)
+    assert normwise(cap.numpy(0), want) <= 2e-3
+    with pytest.raises(RuntimeError, match="all-reduce"):
+        tl.Plan([tl.all_reduce_sum(s)]).capture()

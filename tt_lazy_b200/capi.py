@@ -68,7 +68,7 @@ class MemoryStats(C.Structure):
 
 # Every symbol include/tt_cuda.h declares (checked by tests/test_capi.py).
 EXPORTS = ["ttc_last_error", "ttc_init", "ttc_shutdown", "ttc_device_count", "ttc_version", "ttc_get_stream",
-           "ttc_set_stream", "ttc_synchronize", "ttc_malloc", "ttc_free", "ttc_memcpy_h2d", "ttc_memcpy_d2h", "ttc_h2d_prefetch", "ttc_wait_ticket",
+           "ttc_set_stream", "ttc_synchronize", "ttc_malloc", "ttc_free", "ttc_memcpy_h2d", "ttc_memcpy_d2h", "ttc_h2d_prefetch", "ttc_wait_ticket", "ttc_capture_begin", "ttc_capture_end", "ttc_graph_launch", "ttc_graph_destroy",
            "ttc_memcpy_d2d", "ttc_memset_zero", "ttc_host_alloc", "ttc_host_free", "ttc_get_memory_stats",
            "ttc_eltwise_chain", "ttc_eltwise_chain_noalloc", "ttc_chain_jit_source", "ttc_reduce", "ttc_transpose", "ttc_copy2d", "ttc_gemm", "ttc_gemm_select_path",
            "ttc_comm_unique_id", "ttc_comm_init", "ttc_allreduce_sum", "ttc_comm_destroy"]
@@ -99,6 +99,9 @@ def lib():
         L.ttc_memset_zero.argtypes = [C.c_void_p, C.c_size_t]
         L.ttc_h2d_prefetch.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, C.POINTER(C.c_int)]
         L.ttc_wait_ticket.argtypes = [C.c_int]
+        L.ttc_capture_end.argtypes = [C.POINTER(C.c_void_p)]
+        L.ttc_graph_launch.argtypes = [C.c_void_p]
+        L.ttc_graph_destroy.argtypes = [C.c_void_p]
         L.ttc_host_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)]
         L.ttc_host_free.argtypes = [C.c_void_p]
         L.ttc_set_stream.argtypes = [C.c_void_p]

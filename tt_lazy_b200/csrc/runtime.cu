@@ -393,6 +393,38 @@ int ttc_wait_ticket(int ticket) {
     return TTC_OK;
 }
 
+int ttc_capture_begin(void) {
+    TTC_REQUIRE_INIT();
+    TTC_CUDA(cudaStreamBeginCapture(rt().stream, cudaStreamCaptureModeThreadLocal));
+    return TTC_OK;
+}
+
+int ttc_capture_end(void** graph_exec) {
+    TTC_REQUIRE_INIT();
+    if (!graph_exec) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: capture_end: graph_exec is NULL");
+    *graph_exec = nullptr;
+    cudaGraph_t g = nullptr;
+    TTC_CUDA(cudaStreamEndCapture(rt().stream, &g));
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t e = cudaGraphInstantiateWithFlags(&exec, g, cudaGraphInstantiateFlagAutoFreeOnLaunch);
+    cudaGraphDestroy(g);
+    TTC_CUDA(e);
+    *graph_exec = (void*)exec;
+    return TTC_OK;
+}
+
+int ttc_graph_launch(void* graph_exec) {
+    TTC_REQUIRE_INIT();
+    if (!graph_exec) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: graph_launch: NULL graph");
+    TTC_CUDA(cudaGraphLaunch((cudaGraphExec_t)graph_exec, rt().stream));
+    return TTC_OK;
+}
+
+int ttc_graph_destroy(void* graph_exec) {
+    if (graph_exec) cudaGraphExecDestroy((cudaGraphExec_t)graph_exec);
+    return TTC_OK;
+}
+
 int ttc_memcpy_d2h(void* dst, const void* src, size_t bytes) {
     TTC_REQUIRE_INIT();
     if (bytes == 0) return TTC_OK;

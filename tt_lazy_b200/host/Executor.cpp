@@ -91,7 +91,9 @@ std::shared_ptr<DeviceBuffer> MemoryManager::allocate(size_t bytes) {
     stats_.allocations++;
     stats_.bytes_live += b;
     stats_.bytes_peak = std::max(stats_.bytes_peak, stats_.bytes_live);
-    return std::make_shared<DeviceBuffer>(p, b);
+    auto buf = std::make_shared<DeviceBuffer>(p, b);
+    if (sink_) sink_->push_back(buf);
+    return buf;
 }
 
 void MemoryManager::release(float* ptr, size_t bytes) {
@@ -1103,10 +1105,64 @@ CompiledTape::CompiledTape(const std::vector<Tensor>& outputs, int pipeline_chun
     }
 }
 
+CompiledTape::~CompiledTape() {
+    if (graph_) ttc_graph_destroy(graph_);
+}
+
 void CompiledTape::run() {
     backend_init();
+    if (graph_) {
+        check(ttc_graph_launch(graph_));
+        return;  // results_ and kernels_ are those of the captured run
+    }
     ttc_memory_stats before;
     ttc_get_memory_stats(&before);
+    execute();
+    ttc_memory_stats after;
+    ttc_get_memory_stats(&after);
+    kernels_ = (size_t)(after.kernels_launched - before.kernels_launched);
+}
+
+void CompiledTape::capture() {
+    if (graph_) return;
+    for (const auto& op : tape_->operations())
+        if (op->op_type == AllReduceArgs::type_id())
+            throw std::runtime_error("Plan.capture: a plan with an all-reduce is not captured (it waits on the host)");
+    run();  // warm: specialised kernels compiled, scratch grown, buffer pool filled
+    check(ttc_synchronize());
+    std::vector<std::shared_ptr<DeviceBuffer>> held;
+    MemoryManager::instance().set_capture_sink(&held);
+    const auto mm0 = MemoryManager::instance().stats();
+    ttc_memory_stats before;
+    ttc_get_memory_stats(&before);
+    check(ttc_capture_begin());
+    void* exec = nullptr;
+    try {
+        execute();
+    } catch (...) {
+        ttc_capture_end(&exec);  // ends the (now invalid) capture
+        ttc_graph_destroy(exec);
+        MemoryManager::instance().set_capture_sink(nullptr);
+        throw;
+    }
+    const int rc = ttc_capture_end(&exec);
+    MemoryManager::instance().set_capture_sink(nullptr);
+    check(rc);
+    // every buffer of the recorded run must come from the pool the warm run
+    // filled: a fresh stream-ordered allocation would belong to the graph
+    const auto mm1 = MemoryManager::instance().stats();
+    if (mm1.allocations - mm0.allocations != mm1.reuses - mm0.reuses) {
+        ttc_graph_destroy(exec);
+        throw std::runtime_error("Plan.capture: the recorded run needed new device memory; run it uncaptured");
+    }
+    ttc_memory_stats after;
+    ttc_get_memory_stats(&after);
+    kernels_ = (size_t)(after.kernels_launched - before.kernels_launched);
+    graph_ = exec;
+    graph_bufs_ = std::move(held);
+}
+
+void CompiledTape::execute() {
     for (const auto& op : tape_->operations()) op->is_evaluated = false;
     results_.clear();
     executor_.clear_results();
@@ -1130,9 +1186,6 @@ void CompiledTape::run() {
         results_.push_back(r);
     }
     executor_.clear_results();
-    ttc_memory_stats after;
-    ttc_get_memory_stats(&after);
-    kernels_ = (size_t)(after.kernels_launched - before.kernels_launched);
 }
 
 std::shared_ptr<Tensor> CompiledTape::result(size_t i) const { return results_.at(i); }

@@ -94,10 +94,14 @@ class MemoryManager {
     void reset_peak() { stats_.bytes_peak = stats_.bytes_live; }
     // Host buffers of >= 1 MiB are pinned (page-locked) once the backend is up.
     static std::shared_ptr<float> host_buffer(size_t n);
+    // While a sink is set, every allocation is also kept in it, so buffers
+    // a captured CUDA graph writes are never handed to other work.
+    void set_capture_sink(std::vector<std::shared_ptr<DeviceBuffer>>* sink) { sink_ = sink; }
 
    private:
     std::unordered_map<size_t, std::vector<float*>> free_;
     Stats stats_;
+    std::vector<std::shared_ptr<DeviceBuffer>>* sink_ = nullptr;
 };
 
 // Device copies of constant tensors (host pointer + size -> device buffer),
@@ -168,7 +172,17 @@ void evaluate(std::vector<Tensor*> tensors);
 class CompiledTape {
    public:
     explicit CompiledTape(const std::vector<Tensor>& outputs, int pipeline_chunks = 1);
+    ~CompiledTape();
+    CompiledTape(const CompiledTape&) = delete;
+    CompiledTape& operator=(const CompiledTape&) = delete;
     void run();
+    // Runs once, then records one run into a CUDA graph; from then on run()
+    // replays the graph with a single launch (same inputs, same device
+    // buffers; streamed inputs are still copied from their host memory on
+    // every replay). Plans with an all-reduce are not captured (it waits on
+    // the host).
+    void capture();
+    bool captured() const { return graph_ != nullptr; }
     std::shared_ptr<Tensor> result(size_t i) const;
     size_t size() const { return tape_->size(); }
     size_t kernels_last_run() const { return kernels_; }
@@ -181,6 +195,9 @@ class CompiledTape {
     std::vector<std::shared_ptr<Tensor>> results_;
     std::vector<Tensor> prefetch_;  // streamed chunk inputs uploaded on the copy stream
     size_t kernels_ = 0;
+    void execute();
+    void* graph_ = nullptr;                                  // ttc graph exec of the captured run
+    std::vector<std::shared_ptr<DeviceBuffer>> graph_bufs_;  // every buffer the graph touches
 };
 
 // Row-chunked form of `outputs` over their one streamed rank-2 batch input

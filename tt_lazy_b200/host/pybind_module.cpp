@@ -104,6 +104,8 @@ PYBIND11_MODULE(_tt_lazy, m) {
     py::class_<tt_lazy::CompiledTape>(m, "Plan")
         .def(py::init<const std::vector<Tensor>&, int>(), py::arg("outputs"), py::arg("pipeline_chunks") = 1)
         .def("run", &tt_lazy::CompiledTape::run, py::call_guard<py::gil_scoped_release>())
+        .def("capture", &tt_lazy::CompiledTape::capture, py::call_guard<py::gil_scoped_release>())
+        .def_property_readonly("captured", &tt_lazy::CompiledTape::captured)
         .def("numpy",
              [](const tt_lazy::CompiledTape& p, size_t i) {
                  Tensor t = *p.result(i);
