@@ -91,9 +91,20 @@ std::shared_ptr<DeviceBuffer> MemoryManager::allocate(size_t bytes) {
     stats_.allocations++;
     stats_.bytes_live += b;
     stats_.bytes_peak = std::max(stats_.bytes_peak, stats_.bytes_live);
-    auto buf = std::make_shared<DeviceBuffer>(p, b);
-    if (sink_) sink_->push_back(buf);
-    return buf;
+    if (recording_) recorded_.emplace_back(p, b);
+    return std::make_shared<DeviceBuffer>(p, b);
+}
+
+std::shared_ptr<DeviceBuffer> MemoryManager::claim(float* ptr, size_t bytes) {
+    auto it = free_.find(bytes);
+    if (it == free_.end()) return nullptr;
+    auto& v = it->second;
+    auto pos = std::find(v.begin(), v.end(), ptr);
+    if (pos == v.end()) return nullptr;
+    v.erase(pos);
+    stats_.bytes_cached -= bytes;
+    stats_.bytes_live += bytes;
+    return std::make_shared<DeviceBuffer>(ptr, bytes);
 }
 
 void MemoryManager::release(float* ptr, size_t bytes) {
@@ -1130,9 +1141,9 @@ void CompiledTape::capture() {
             throw std::runtime_error("Plan.capture: a plan with an all-reduce is not captured (it waits on the host)");
     run();  // warm: specialised kernels compiled, scratch grown, buffer pool filled
     check(ttc_synchronize());
-    std::vector<std::shared_ptr<DeviceBuffer>> held;
-    MemoryManager::instance().set_capture_sink(&held);
-    const auto mm0 = MemoryManager::instance().stats();
+    auto& mm = MemoryManager::instance();
+    mm.begin_record();
+    const auto mm0 = mm.stats();
     ttc_memory_stats before;
     ttc_get_memory_stats(&before);
     check(ttc_capture_begin());
@@ -1142,19 +1153,25 @@ void CompiledTape::capture() {
     } catch (...) {
         ttc_capture_end(&exec);  // ends the (now invalid) capture
         ttc_graph_destroy(exec);
-        MemoryManager::instance().set_capture_sink(nullptr);
+        mm.end_record();
         throw;
     }
     const int rc = ttc_capture_end(&exec);
-    MemoryManager::instance().set_capture_sink(nullptr);
+    const auto used = mm.end_record();
     check(rc);
     // every buffer of the recorded run must come from the pool the warm run
     // filled: a fresh stream-ordered allocation would belong to the graph
-    const auto mm1 = MemoryManager::instance().stats();
+    const auto mm1 = mm.stats();
     if (mm1.allocations - mm0.allocations != mm1.reuses - mm0.reuses) {
         ttc_graph_destroy(exec);
         throw std::runtime_error("Plan.capture: the recorded run needed new device memory; run it uncaptured");
     }
+    // Buffers the recorded run released (intermediates, reused within the
+    // graph in stream order) leave the pool for good; the rest are the
+    // results, which this plan holds.
+    std::vector<std::shared_ptr<DeviceBuffer>> held;
+    for (const auto& [ptr, bytes] : used)
+        if (auto b = mm.claim(ptr, bytes)) held.push_back(std::move(b));
     ttc_memory_stats after;
     ttc_get_memory_stats(&after);
     kernels_ = (size_t)(after.kernels_launched - before.kernels_launched);
@@ -1163,7 +1180,10 @@ void CompiledTape::capture() {
 }
 
 void CompiledTape::execute() {
-    for (const auto& op : tape_->operations()) op->is_evaluated = false;
+    for (const auto& op : tape_->operations()) {
+        op->is_evaluated = false;
+        op->result.reset();  // the previous run's result buffers go back to the pool
+    }
     results_.clear();
     executor_.clear_results();
     // start every chunk's upload on the copy stream; chunk c's kernels wait for chunk c only

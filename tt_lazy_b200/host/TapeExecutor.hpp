@@ -94,14 +94,25 @@ class MemoryManager {
     void reset_peak() { stats_.bytes_peak = stats_.bytes_live; }
     // Host buffers of >= 1 MiB are pinned (page-locked) once the backend is up.
     static std::shared_ptr<float> host_buffer(size_t n);
-    // While a sink is set, every allocation is also kept in it, so buffers
-    // a captured CUDA graph writes are never handed to other work.
-    void set_capture_sink(std::vector<std::shared_ptr<DeviceBuffer>>* sink) { sink_ = sink; }
+    // Recording (CUDA-graph capture): every allocation between begin_record
+    // and end_record is listed; claim() then takes a listed buffer that is
+    // back in the pool out of it for good (the graph writes it on every
+    // replay), handing ownership to the caller.
+    void begin_record() {
+        recording_ = true;
+        recorded_.clear();
+    }
+    std::vector<std::pair<float*, size_t>> end_record() {
+        recording_ = false;
+        return std::move(recorded_);
+    }
+    std::shared_ptr<DeviceBuffer> claim(float* ptr, size_t bytes);
 
    private:
     std::unordered_map<size_t, std::vector<float*>> free_;
     Stats stats_;
-    std::vector<std::shared_ptr<DeviceBuffer>>* sink_ = nullptr;
+    bool recording_ = false;
+    std::vector<std::pair<float*, size_t>> recorded_;
 };
 
 // Device copies of constant tensors (host pointer + size -> device buffer),
