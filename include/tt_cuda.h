@@ -253,7 +253,13 @@ int ttc_copy2d(const float* in, int64_t in_ld, float* out, int64_t out_ld, int64
  * starts as the product (no LOAD needed): e.g. ADD INPUT 0 (bias view with
  * row_stride 0), RELU, STORE 0 is the fused MLP layer. rows/cols/nseg of the
  * epilogue are ignored (M, N, 1 are used). An epilogue with n_instr == 0
- * means STORE to `c`.
+ * means STORE to `c` (or nothing when `c` is NULL and a reduction is set).
+ * The epilogue's `reduce` may be TTC_REDUCE_COLS: reduce_out[n] = the sum
+ * (mean with reduce_mean) over the M rows of the epilogue's final value, the
+ * batch-dim reduce_sum of the reference's handle_reduce on the GEMM result
+ * (reduce_sum.cpp:9-62) without writing that [M, N] value anywhere. The TF32
+ * kernels sum each 32-row group in the epilogue (deterministic, no atomics)
+ * and combine the groups in fp64; the FFMA path reduces a scratch copy.
  *
  * path: TTC_GEMM_FFMA -- fp32 CUDA-core FMA (norm-wise rel. error ~1e-6,
  *                         the 1e-5 bound);

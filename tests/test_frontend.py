@@ -71,9 +71,11 @@ def test_mlp_fusion_absorbs_bias_and_activation():
     h = tl.relu(tl.add(tl.matmul(X, W1), b1))
     y = tl.add(tl.matmul(h, W2), b2)
     m = tl.reduce_mean(y, [0])
-    assert ops([m]) == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add]", "Reduce"]
+    # the batch-dim mean becomes the second GEMM's epilogue column sum
+    assert ops([m]) == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add -> reduce]"]
     # an intermediate requested as an output is not absorbed
-    assert ops([m, h])[:2] == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add]"]
+    assert ops([m, h]) == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add -> reduce]"]
+    assert ops([m, y]) == ["FusedGemm[matmul -> add -> relu]", "FusedGemm[matmul -> add]", "Reduce"]
     tl.set_optimization(False)
     try:
         assert ops([m]) == ["MatMul", "Add", "ReLU", "MatMul", "Add", "Reduce"]
@@ -85,7 +87,10 @@ def test_large_mlp_sigmoid_then_batch_sum():
     X, W1, W2 = c((64, 32)), c((32, 128)), c((128, 32))
     y = tl.sigmoid(tl.matmul(tl.relu(tl.matmul(X, W1)), W2))
     s = tl.reduce_sum(y, [0])
-    assert ops([s]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid]", "Reduce"]
+    assert ops([s]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid -> reduce]"]
+    # a reduction over the other dim is not a column sum: it stays a chain
+    r = tl.reduce_sum(y, [1])
+    assert ops([r]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid]", "Reduce"]
 
 
 def test_bandwidth_graph_views_and_chains():
@@ -151,12 +156,12 @@ def test_pipelined_plan_rebuilds_the_graph_over_row_chunks():
     xs = tl.streamed(X)
     W1, W2 = c((16, 32), 1), c((32, 8), 2)
     s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xs, W1)), W2)), [0])
-    assert ops([s]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid]", "Reduce"]
-    assert len(tl.Plan([s])) == 3
-    # 4 chunks x (GEMM, GEMM, partial sum) + the chunk-order sum of the partials (one fused chain)
-    assert len(tl.Plan([s], pipeline_chunks=4)) == 13
+    assert ops([s]) == ["FusedGemm[matmul -> relu]", "FusedGemm[matmul -> sigmoid -> reduce]"]
+    assert len(tl.Plan([s])) == 2
+    # 4 chunks x (GEMM, GEMM with the partial column sum) + the chunk-order sum of the partials (one chain)
+    assert len(tl.Plan([s], pipeline_chunks=4)) == 9
     # the all-reduce runs once, after the partial sums are combined
-    assert len(tl.Plan([tl.all_reduce_sum(s)], pipeline_chunks=3)) == 11
+    assert len(tl.Plan([tl.all_reduce_sum(s)], pipeline_chunks=3)) == 8
 
 
 def test_pipelined_plan_rejects_graphs_that_are_not_row_local():

@@ -350,3 +350,48 @@ def test_invalid_descriptors_are_errors(ttc):
         ttc.eltwise_chain(bad)
     with pytest.raises(ttc.TTCError):
         ttc.gemm(4, 4, 4, X.ptr, 2, X.ptr, 4, X.ptr, 4)
+
+
+@pytest.mark.parametrize("path", ["ffma", "tf32", "tf32_pair"])
+@pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (1000, 260, 772), (520, 64, 1032)])
+@pytest.mark.parametrize("mean,store", [(False, False), (True, True)])
+def test_gemm_epilogue_column_sum(ttc, path, m, k, n, mean, store, monkeypatch):
+    """Epilogue reduction TTC_REDUCE_COLS: the column sums (or means) over the
+    M rows of the final epilogue value, from per-32-row partials written by
+    the epilogue (TF32 kernels) or a column-sum chain (FFMA path); with STORE
+    the matrix is written as well."""
+    if path == "tf32_pair":
+        monkeypatch.setenv("TTC_GEMM_PAIR", "1")
+    rng = np.random.default_rng(14)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, (1, n)).astype(np.float32)
+    A, B, Bv = dev(ttc, a), dev(ttc, b), dev(ttc, bias)
+    S = ttc.DeviceArray.empty((n,))
+    C = ttc.DeviceArray.empty((m, n))
+    prog = [ttc.instr(ttc.OP_ADD, ttc.SRC_INPUT, 0), ttc.instr(ttc.OP_SIGMOID)]
+    outs = []
+    if store:
+        prog.append(ttc.instr(ttc.OP_STORE, idx=0))
+        outs = [ttc.out_view(C.ptr, n)]
+    epi = ttc.chain_desc(m, n, [ttc.in_view(Bv.ptr, 0)], outs, prog, reduce=ttc.REDUCE_COLS, reduce_out=S.ptr,
+                         mean=mean)
+    p = ttc.GEMM_FFMA if path == "ffma" else ttc.GEMM_TF32
+    ttc.gemm(m, n, k, A.ptr, k, B.ptr, n, path=p, epilogue=epi)
+    y = oracle.sigmoid(oracle.add(oracle.matmul(a, b), bias))
+    want = oracle.reduce(y, (0,), mean=mean, f64=True)
+    tol = RTOL_FFMA if path == "ffma" else RTOL_TF32
+    assert normwise(S.numpy(), want) <= tol
+    if store:
+        assert normwise(C.numpy(), y) <= tol
+
+
+def test_gemm_epilogue_column_sum_of_no_rows(ttc):
+    A = ttc.DeviceArray.empty((1, 8))
+    B = ttc.DeviceArray.empty((8, 16))
+    S = ttc.DeviceArray.empty((16,))
+    for mean, want in ((False, 0.0), (True, np.nan)):
+        epi = ttc.chain_desc(0, 16, [], [], [], reduce=ttc.REDUCE_COLS, reduce_out=S.ptr, mean=mean)
+        ttc.gemm(0, 16, 8, A.ptr, 8, B.ptr, 16, epilogue=epi)
+        got = S.numpy()
+        assert np.all(np.isnan(got)) if mean else np.all(got == 0.0)

@@ -19,8 +19,9 @@
 
 namespace ttc {
 
-int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi);
+int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean);
 bool tf32_supported(const ttc_gemm_desc& d, const DProgram& epi, bool epi_vec);
+int run_chain(const ttc_chain_desc& d);
 
 namespace {
 
@@ -187,12 +188,15 @@ bool epilogue_vec_ok(const ttc_chain_desc& e, int N) {
     return true;
 }
 
-// Builds the effective epilogue: an empty program means "STORE to c".
+// Builds the effective epilogue: an empty program means "STORE to c" (or
+// nothing, when only the column sum of the product is asked for).
 int make_epilogue(const ttc_gemm_desc& d, ttc_chain_desc* e) {
     *e = d.epilogue;
-    if (e->reduce != TTC_REDUCE_NONE)
-        return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: GEMM epilogue reductions are not supported");
-    if (e->n_instr == 0) {
+    if (e->reduce != TTC_REDUCE_NONE && e->reduce != TTC_REDUCE_COLS)
+        return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: a GEMM epilogue reduces over rows (TTC_REDUCE_COLS) only");
+    if (e->reduce == TTC_REDUCE_COLS && !e->reduce_out)
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: GEMM epilogue reduction without reduce_out");
+    if (e->n_instr == 0 && !(e->reduce == TTC_REDUCE_COLS && !d.c)) {
         if (!d.c) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: GEMM with no epilogue needs c");
         if (e->n_outputs != 0)
             return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: empty GEMM epilogue with outputs");
@@ -243,12 +247,65 @@ int ttc_gemm(const ttc_gemm_desc* desc) {
     if (int rc = validate_gemm(d)) return rc;
     ttc_chain_desc e;
     if (int rc = make_epilogue(d, &e)) return rc;
-    if (d.M == 0 || d.N == 0) return TTC_OK;
+    const bool reduce = e.reduce == TTC_REDUCE_COLS;
+    if (d.M == 0 || d.N == 0) {
+        if (!reduce || d.N == 0) return TTC_OK;
+        ttc_chain_desc z;  // column sums over no rows: 0 (NaN for a mean); the input is never read
+        std::memset(&z, 0, sizeof z);
+        z.rows = 0;
+        z.cols = d.N;
+        z.nseg = 1;
+        z.n_inputs = 1;
+        z.inputs[0] = ttc_in_view{e.reduce_out, d.N, 1, 0};
+        z.n_instr = 1;
+        z.program[0] = ttc_instr{TTC_OP_LOAD, TTC_SRC_INPUT, 0, 0};
+        z.reduce = TTC_REDUCE_COLS;
+        z.reduce_mean = e.reduce_mean;
+        z.reduce_out = e.reduce_out;
+        return run_chain(z);
+    }
     GemmParams p;
     std::memset(&p, 0, sizeof p);
     if (int rc = decode_program(e, true, &p.epi)) return rc;
     const bool vec = epilogue_vec_ok(e, d.N);
-    if (d.path != TTC_GEMM_FFMA && tf32_supported(d, p.epi, vec)) return run_gemm_tf32(d, p.epi);
+    if (d.path != TTC_GEMM_FFMA && tf32_supported(d, p.epi, vec))
+        return run_gemm_tf32(d, p.epi, reduce ? e.reduce_out : nullptr, e.reduce_mean);
+    if (reduce) {
+        // FFMA path: the final epilogue value goes to a scratch matrix, then
+        // one column-sum chain over it.
+        if (d.path == TTC_GEMM_TF32)
+            return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: TF32 path does not take this GEMM (%d x %d x %d)", d.M,
+                             d.N, d.K);
+        if (e.n_outputs >= TTC_CHAIN_MAX_OUTPUTS || e.n_instr >= TTC_CHAIN_MAX_INSTR)
+            return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: GEMM epilogue too long to add a column sum");
+        float* tmp = nullptr;
+        TTC_CUDA(cudaMallocAsync((void**)&tmp, (size_t)d.M * d.N * sizeof(float), rt().stream));
+        ttc_gemm_desc g = d;
+        g.epilogue = e;
+        g.epilogue.reduce = TTC_REDUCE_NONE;
+        g.epilogue.reduce_out = nullptr;
+        g.epilogue.outputs[g.epilogue.n_outputs] = ttc_out_view{tmp, d.N, 0};
+        g.epilogue.program[g.epilogue.n_instr++] = ttc_instr{TTC_OP_STORE, 0, (uint8_t)g.epilogue.n_outputs++, 0};
+        g.path = TTC_GEMM_FFMA;
+        int rc = ttc_gemm(&g);
+        if (rc == TTC_OK) {
+            ttc_chain_desc r;
+            std::memset(&r, 0, sizeof r);
+            r.rows = d.M;
+            r.cols = d.N;
+            r.nseg = 1;
+            r.n_inputs = 1;
+            r.inputs[0] = ttc_in_view{tmp, d.N, 1, 0};
+            r.n_instr = 1;
+            r.program[0] = ttc_instr{TTC_OP_LOAD, TTC_SRC_INPUT, 0, 0};
+            r.reduce = TTC_REDUCE_COLS;
+            r.reduce_mean = e.reduce_mean;
+            r.reduce_out = e.reduce_out;
+            rc = run_chain(r);
+        }
+        cudaFreeAsync(tmp, rt().stream);
+        return rc;
+    }
     if (d.path == TTC_GEMM_TF32)
         return set_error(TTC_ERR_UNSUPPORTED,
                          "tt_cuda: TF32 path needs M, N multiples of 128/16 and K of 32 with 16-byte aligned rows "

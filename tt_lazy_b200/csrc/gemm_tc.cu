@@ -53,6 +53,7 @@ struct TcParams {
     unsigned idesc;
     int* status;
     DProgram epi;
+    float* partials;  // column sums of the final epilogue value per 32-row group, or null
 };
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -84,6 +85,36 @@ __device__ __forceinline__ void tc_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[3
         : "r"(taddr));
 }
 __device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Column sums over a warp's 32 rows (one per lane) of 16 consecutive columns
+// (v[g][w] is column 4 g + w; invalid elements already zeroed): a fixed-order
+// transpose reduction, 16 shuffles; lanes 2c and 2c+1 end with column c and
+// the even lane writes it to out[c] when c < ncols (columns past the matrix
+// edge would land in the next row group's partials). Deterministic.
+__device__ __forceinline__ void warp_col_sums16(const float (&v)[4][4], float* out, int lane, long long ncols) {
+    // The epilogue program branches per lane (row validity, sigmoid's range
+    // test): reconverge the warp before the shuffles read other lanes.
+    __syncwarp();
+    float a[16];
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+#pragma unroll
+        for (int w = 0; w < 4; ++w) a[4 * g + w] = v[g][w];
+    const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4, h2 = lane & 2;
+    float b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        b[i] = (h16 ? a[i + 8] : a[i]) + __shfl_xor_sync(0xffffffffu, h16 ? a[i] : a[i + 8], 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        b[i] = (h8 ? b[i + 4] : b[i]) + __shfl_xor_sync(0xffffffffu, h8 ? b[i] : b[i + 4], 8);
+#pragma unroll
+    for (int i = 0; i < 2; ++i)
+        b[i] = (h4 ? b[i + 2] : b[i]) + __shfl_xor_sync(0xffffffffu, h4 ? b[i] : b[i + 2], 4);
+    float c = (h2 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, h2 ? b[0] : b[1], 2);
+    c += __shfl_xor_sync(0xffffffffu, c, 1);
+    if ((lane & 1) == 0 && ((lane >> 1) & 15) < ncols) out[(lane >> 1) & 15] = c;
+}
 
 // Shared-memory matrix descriptor (sm_100 layout: start address, leading /
 // stride byte offsets in 16-byte units, version 1, layout type in bits
@@ -280,6 +311,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                         for (int w = 0; w < 4; ++w) v[g][w] = __uint_as_float(r[h * 16 + g * 4 + w]);
                     }
                     run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
+                    if (p.partials) {
+#pragma unroll
+                        for (int g = 0; g < 4; ++g)
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) v[g][w] = vv[g] ? v[g][w] : 0.0f;
+                        const long long rg = (long long)mb * (BM / 32) + q;
+                        warp_col_sums16(v, p.partials + rg * p.N + col0 + h * 16, lane, p.N - (col0 + h * 16));
+                    }
                 }
             }
             tc_fence_before();
@@ -565,6 +604,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
                         for (int w = 0; w < 4; ++w) v[g][w] = __uint_as_float(r[h * 16 + g * 4 + w]);
                     }
                     run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
+                    if (p.partials) {
+#pragma unroll
+                        for (int g = 0; g < 4; ++g)
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) v[g][w] = vv[g] ? v[g][w] : 0.0f;
+                        const long long rg = (long long)mb2 * (2 * BM / 32) + rank * (BM / 32) + q;
+                        warp_col_sums16(v, p.partials + rg * p.N + col0 + h * 16, lane, p.N - (col0 + h * 16));
+                    }
                 }
             }
             tc_fence_before();
@@ -656,7 +703,13 @@ int launch_pair(TcParams& p) {
 
 }  // namespace
 
-int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi) {
+void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg, float* out, long long sseg, int mean,
+                          double count);
+
+// `reduce_out` (or null): column sums (mean with `mean`) of the final
+// epilogue value over the M rows, from per-32-row partial sums the epilogue
+// writes into the workspace and a fixed-order fp64 finalize.
+int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean) {
     static bool attr_set = false;
     if (!attr_set) {
         TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -696,14 +749,27 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi) {
     p.epi = epi;
     const long long tiles = (long long)p.m_blocks * p.n_blocks;
     if (tiles > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many GEMM tiles");
+    const long long groups = (long long)p.m_blocks * (tm / 32);  // every 32-row group of every row tile
+    if (reduce_out) {
+        if (groups > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many rows for the fused column sum");
+        void* ws = nullptr;
+        if (int rc = workspace((size_t)groups * d.N * sizeof(float), &ws)) return rc;
+        p.partials = (float*)ws;
+    }
     if (pair) {
         if (int rc = launch_pair(p)) return rc;
-        return check_cuda(cudaGetLastError(), "TF32 pair GEMM launch");
+        if (int rc = check_cuda(cudaGetLastError(), "TF32 pair GEMM launch")) return rc;
+    } else {
+        const int grid = (int)(tiles < rt().sm_count ? tiles : rt().sm_count);
+        tf32_gemm_kernel<<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
+        count_launch();
+        if (int rc = check_cuda(cudaGetLastError(), "TF32 GEMM launch")) return rc;
     }
-    const int grid = (int)(tiles < rt().sm_count ? tiles : rt().sm_count);
-    tf32_gemm_kernel<<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
-    count_launch();
-    return check_cuda(cudaGetLastError(), "TF32 GEMM launch");
+    if (reduce_out) {  // rows past M contribute exact zeros
+        launch_finalize_cols(p.partials, (int)groups, d.N, 1, reduce_out, 0, mean, (double)d.M);
+        return check_cuda(cudaGetLastError(), "column-sum finalize launch");
+    }
+    return TTC_OK;
 }
 
 }  // namespace ttc

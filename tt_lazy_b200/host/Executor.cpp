@@ -769,20 +769,34 @@ void run_gemm_plan(TapeOperation& op, TapeExecutor& ex, const FusionPlan& plan, 
         pb.d.inputs[pb.d.n_inputs++] = v;
     }
     std::vector<int> stored;
-    DeviceView out;
+    DeviceView out, red_out;
+    const bool has_reduce = !plan.members.empty() && plan.members.back().op == FusionPlan::REDUCE;
     if (plan.members.empty()) {
         out = new_buffer(out_shape);
         g.c = out.ptr();
         g.ldc = N;
     } else {
         stored = build_program(pb, plan, plan.members.size(), FusionPlan::kProduct);
-        if (stored.size() != 1) throw std::logic_error("fused GEMM must store exactly its final value");
-        out = new_buffer(out_shape);
-        pb.d.outputs[pb.d.n_outputs++] = ttc_out_view{out.ptr(), N, 0};
+        if (stored.size() != (has_reduce ? 0u : 1u))
+            throw std::logic_error("fused GEMM must store exactly its final value");
+        if (!has_reduce) {
+            out = new_buffer(out_shape);
+            pb.d.outputs[pb.d.n_outputs++] = ttc_out_view{out.ptr(), N, 0};
+        } else {  // the batch-dim sum of the final value, reduced in the epilogue
+            const auto& r = plan.members.back();
+            red_out = new_buffer(r.shape);
+            pb.d.reduce = TTC_REDUCE_COLS;
+            pb.d.reduce_mean = r.mean ? 1 : 0;
+            pb.d.reduce_out = red_out.ptr();
+        }
         g.epilogue = pb.d;
     }
     fit_path();
     check(ttc_gemm(&g));
+    if (has_reduce) {
+        set_output(ex, op, plan.members.back().node, 0, plan.members.back().shape, red_out);
+        return;
+    }
     const NodeId node = plan.members.empty() ? op.node_id : plan.members[(size_t)stored[0]].node;
     set_output(ex, op, node, 0, out_shape, out);
 }

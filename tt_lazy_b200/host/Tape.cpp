@@ -475,12 +475,39 @@ int MLPFusionPass::apply(Tape& tape, const std::vector<Tensor>& outputs) {
             }
             if (plan->members.empty()) continue;  // a lone matmul stays a matmul
         }
-        auto op = std::make_unique<TapeOperation>(last, FusedGemmArgs::type_id());
-        op->output_nodes = {last};
-        op->output_shapes = {plan->matmul_shape};
-        set_inputs(*op, *plan);
         if (!plan->members.empty() && plan->members.back().node == 0) plan->members.back().node = last;
         plan->members.back().escapes = true;
+        std::vector<uint32_t> out_shape_of_op = plan->matmul_shape;
+        // A batch-dim (row) reduce_sum / reduce_mean that alone reads the
+        // final value becomes the epilogue's column sum: the [M, N] value is
+        // then never written to memory.
+        const long red = single_private_use(last);
+        if (red >= 0 && group_of[(size_t)red] < 0 && kind_of(*ops[(size_t)red]) == Kind::REDUCE &&
+            plan->matmul_shape.size() == 2) {
+            TapeOperation& rop = *ops[(size_t)red];
+            const auto& ra = Context::instance().get_node(rop.node_id)->as<ReduceArgs>();
+            const bool rows_only = ra.dims.size() == 1 && (ra.dims[0] == 0 || ra.dims[0] == -2);
+            if (rows_only && (ra.type == ReduceArgs::Type::SUM || ra.type == ReduceArgs::Type::MEAN)) {
+                plan->members.back().escapes = false;
+                FusionPlan::Member r;
+                r.node = rop.node_id;
+                r.op = FusionPlan::REDUCE;
+                r.args = {(int)plan->members.size() - 1};
+                r.shape = out_shape(rop);
+                r.dims.assign(ra.dims.begin(), ra.dims.end());
+                r.keepdim = ra.keepdim;
+                r.mean = ra.type == ReduceArgs::Type::MEAN;
+                r.escapes = true;
+                plan->members.push_back(r);
+                absorbed.push_back((size_t)red);
+                last = rop.node_id;
+                out_shape_of_op = r.shape;
+            }
+        }
+        auto op = std::make_unique<TapeOperation>(last, FusedGemmArgs::type_id());
+        op->output_nodes = {last};
+        op->output_shapes = {out_shape_of_op};
+        set_inputs(*op, *plan);
         op->plan = plan;
         const int g = (int)fused.size();
         for (size_t a : absorbed) group_of[a] = g;
