@@ -91,6 +91,14 @@ int ttc_capture_begin(void);
 int ttc_capture_end(void** graph_exec);
 int ttc_graph_launch(void* graph_exec);
 int ttc_graph_destroy(void* graph_exec);
+/* Tracing (no reference counterpart; the reference only logs): NVTX ranges
+ * around tape operations for an attached profiler, and CUDA-event marks on
+ * the library stream. ttc_timer_elapsed waits for mark `to` and returns the
+ * device time between the two marks. Marks come from a ring of 4096. */
+int ttc_range_push(const char* name);
+int ttc_range_pop(void);
+int ttc_timer_mark(int* mark);
+int ttc_timer_elapsed(int from, int to, float* ms);
 int ttc_memcpy_d2d(void* dst, const void* src, size_t bytes);
 int ttc_memset_zero(void* dst, size_t bytes);
 /* Pinned host memory for staging (cudaHostAlloc). */

@@ -403,3 +403,28 @@ def test_captured_pipelined_mlp_plan():
     assert normwise(cap.numpy(0), want) <= 2e-3
     with pytest.raises(RuntimeError, match="all-reduce"):
         tl.Plan([tl.all_reduce_sum(s)]).capture()
+
+
+def test_profiling_times_every_tape_operation():
+    """set_profiling(True): each tape operation runs between two CUDA-event
+    marks inside an NVTX range named after it; profile() lists them in tape
+    order with their device times."""
+    rng = np.random.default_rng(43)
+    X = rng.standard_normal((512, 256)).astype(np.float32)
+    W1 = (rng.standard_normal((256, 512)) / 16).astype(np.float32)
+    W2 = (rng.standard_normal((512, 128)) / np.sqrt(512)).astype(np.float32)
+    s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(tl.constant(X), tl.constant(W1))), tl.constant(W2))),
+                      [0])
+    names = [o["op"] for o in tl.tape([s])]
+    tl.set_profiling(True)
+    try:
+        plan = tl.Plan([s])
+        plan.run()
+        prof = tl.profile()
+    finally:
+        tl.set_profiling(False)
+    assert [p["op"] for p in prof] == names
+    assert all(p["ms"] > 0 for p in prof)
+    plan.capture()  # recording turns the marks off by itself
+    plan.run()
+    assert tl.profile() == prof or len(tl.profile()) == len(prof)

@@ -8,7 +8,7 @@ sm_100a CUDA backend ``tt_cuda_lib`` (``csrc/``, C-ABI in ``include/tt_cuda.h``)
   ``reduce_sum``, ``reduce_mean``, ``fused_mlp``, ``evaluate``, ``tape``,
   ``stats`` -- re-exported from the pybind11 module over the C++ classes.
 
-Both load in-tree shared objects built by ``python -m tt_lazy_b200.build``;
+Both load in-tree shared objects built by ``python tt_lazy_b200/build.py``;
 a missing build is an ImportError, never a CPU fallback.
 """
 from . import capi  # noqa: F401
@@ -16,7 +16,7 @@ from . import capi  # noqa: F401
 try:
     from . import _tt_lazy as _fe
 except ImportError as e:  # pragma: no cover - only before the first build
-    raise ImportError(f"tt_lazy_b200 front end not built ({e}); run python -m tt_lazy_b200.build") from e
+    raise ImportError(f"tt_lazy_b200 front end not built ({e}); run python tt_lazy_b200/build.py") from e
 
 Tensor = _fe.Tensor
 constant = _fe.constant
@@ -48,3 +48,5 @@ comm_init = _fe.comm_init
 comm_destroy = _fe.comm_destroy
 Plan = _fe.Plan
 stream = _fe.stream
+set_profiling = _fe.set_profiling
+profile = _fe.profile

@@ -68,7 +68,7 @@ class MemoryStats(C.Structure):
 
 # Every symbol include/tt_cuda.h declares (checked by tests/test_capi.py).
 EXPORTS = ["ttc_last_error", "ttc_init", "ttc_shutdown", "ttc_device_count", "ttc_version", "ttc_get_stream",
-           "ttc_set_stream", "ttc_synchronize", "ttc_malloc", "ttc_free", "ttc_memcpy_h2d", "ttc_memcpy_d2h", "ttc_h2d_prefetch", "ttc_wait_ticket", "ttc_capture_begin", "ttc_capture_end", "ttc_graph_launch", "ttc_graph_destroy",
+           "ttc_set_stream", "ttc_synchronize", "ttc_malloc", "ttc_free", "ttc_memcpy_h2d", "ttc_memcpy_d2h", "ttc_h2d_prefetch", "ttc_wait_ticket", "ttc_capture_begin", "ttc_capture_end", "ttc_graph_launch", "ttc_graph_destroy", "ttc_range_push", "ttc_range_pop", "ttc_timer_mark", "ttc_timer_elapsed",
            "ttc_memcpy_d2d", "ttc_memset_zero", "ttc_host_alloc", "ttc_host_free", "ttc_get_memory_stats",
            "ttc_eltwise_chain", "ttc_eltwise_chain_noalloc", "ttc_chain_jit_source", "ttc_reduce", "ttc_transpose", "ttc_copy2d", "ttc_gemm", "ttc_gemm_select_path",
            "ttc_comm_unique_id", "ttc_comm_init", "ttc_allreduce_sum", "ttc_comm_destroy"]
@@ -88,7 +88,7 @@ def lib():
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
-            raise ImportError(f"tt_cuda library not built: {LIB_PATH} (run python -m tt_lazy_b200.build)")
+            raise ImportError(f"tt_cuda library not built: {LIB_PATH} (run python tt_lazy_b200/build.py)")
         L = C.CDLL(LIB_PATH, mode=C.RTLD_GLOBAL)
         L.ttc_last_error.restype = C.c_char_p
         L.ttc_get_stream.restype = C.c_void_p
@@ -102,6 +102,9 @@ def lib():
         L.ttc_capture_end.argtypes = [C.POINTER(C.c_void_p)]
         L.ttc_graph_launch.argtypes = [C.c_void_p]
         L.ttc_graph_destroy.argtypes = [C.c_void_p]
+        L.ttc_range_push.argtypes = [C.c_char_p]
+        L.ttc_timer_mark.argtypes = [C.POINTER(C.c_int)]
+        L.ttc_timer_elapsed.argtypes = [C.c_int, C.c_int, C.POINTER(C.c_float)]
         L.ttc_host_alloc.argtypes = [C.c_size_t, C.POINTER(C.c_void_p)]
         L.ttc_host_free.argtypes = [C.c_void_p]
         L.ttc_set_stream.argtypes = [C.c_void_p]

@@ -7,6 +7,8 @@
 #include <cstring>
 #include <unordered_map>
 
+#include <nvtx3/nvToolsExt.h>
+
 #include "tma_util.cuh"
 
 namespace ttc {
@@ -390,6 +392,43 @@ int ttc_wait_ticket(int ticket) {
     if (ticket < 0 || ticket >= 256 || !r.copy_stream)
         return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: wait_ticket: no prefetch %d", ticket);
     TTC_CUDA(cudaStreamWaitEvent(r.stream, r.tickets[ticket], 0));
+    return TTC_OK;
+}
+
+// ------------------------------------------------------------ tracing
+// NVTX ranges (visible to any attached profiler; no-ops otherwise) and
+// CUDA-event marks on the library stream, from a ring of 4096 events.
+namespace {
+cudaEvent_t g_marks[4096] = {};
+unsigned g_next_mark = 0;
+}  // namespace
+
+int ttc_range_push(const char* name) {
+    nvtxRangePushA(name ? name : "");
+    return TTC_OK;
+}
+
+int ttc_range_pop(void) {
+    nvtxRangePop();
+    return TTC_OK;
+}
+
+int ttc_timer_mark(int* mark) {
+    TTC_REQUIRE_INIT();
+    if (!mark) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: timer_mark: mark is NULL");
+    const unsigned i = g_next_mark++ % 4096u;
+    if (!g_marks[i]) TTC_CUDA(cudaEventCreate(&g_marks[i]));
+    TTC_CUDA(cudaEventRecord(g_marks[i], rt().stream));
+    *mark = (int)i;
+    return TTC_OK;
+}
+
+int ttc_timer_elapsed(int from, int to, float* ms) {
+    TTC_REQUIRE_INIT();
+    if (!ms || from < 0 || to < 0 || from >= 4096 || to >= 4096 || !g_marks[from] || !g_marks[to])
+        return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: timer_elapsed: unknown mark");
+    TTC_CUDA(cudaEventSynchronize(g_marks[to]));
+    TTC_CUDA(cudaEventElapsedTime(ms, g_marks[from], g_marks[to]));
     return TTC_OK;
 }
 

@@ -232,8 +232,35 @@ void TapeExecutor::execute_operation(TapeOperation& op) {
     ++ops_executed_;
 }
 
+namespace tt_lazy {
+namespace {
+int g_profiling = -1;  // -1: from TT_LAZY_PROFILE on first use
+std::vector<OpProfile> g_last_profile;
+}  // namespace
+
+void set_profiling(bool on) { g_profiling = on ? 1 : 0; }
+bool profiling() {
+    if (g_profiling < 0) {
+        const char* e = getenv("TT_LAZY_PROFILE");
+        g_profiling = (e && e[0] == '1') ? 1 : 0;
+    }
+    return g_profiling == 1;
+}
+std::vector<OpProfile> last_profile() { return g_last_profile; }
+
+std::string op_label(const TapeOperation& op) {
+    if (op.plan)
+        return std::string(op.plan->has_matmul ? "FusedGemm" : "FusedChain") + "[" + op.plan->describe() + "]";
+    const Node* n = Context::instance().get_node(op.node_id);
+    return n ? std::string(n->op_name()) : std::string("?");
+}
+}  // namespace tt_lazy
+
 void TapeExecutor::execute_tape(Tape& tape) {
     const auto& ops = tape.operations();
+    const bool prof = tt_lazy::profiling();
+    std::vector<std::pair<int, int>> marks;
+    std::vector<std::string> labels;
     std::map<std::pair<NodeId, uint16_t>, size_t> last_use;
     for (size_t i = 0; i < ops.size(); ++i)
         for (const auto& o : ops[i]->operands)
@@ -242,13 +269,34 @@ void TapeExecutor::execute_tape(Tape& tape) {
     for (const auto& t : tape.outputs())
         if (t.is_lazy()) keep.insert({t.producer_node(), t.output_index()});
     for (size_t i = 0; i < ops.size(); ++i) {
+        if (prof) {
+            labels.push_back(tt_lazy::op_label(*ops[i]));
+            int m0 = -1;
+            if (ttc_timer_mark(&m0) != TTC_OK) throw std::runtime_error(ttc_last_error());
+            ttc_range_push(labels.back().c_str());
+            marks.push_back({m0, -1});
+        }
         execute_operation(*ops[i]);
+        if (prof) {
+            ttc_range_pop();
+            if (ttc_timer_mark(&marks.back().second) != TTC_OK) throw std::runtime_error(ttc_last_error());
+        }
         // release operands whose last reader just ran
         for (const auto& o : ops[i]->operands) {
             if (!o.lazy) continue;
             const auto key = std::make_pair(o.node, o.index);
             if (last_use[key] == i && !keep.count(key)) results_.erase(key);
         }
+    }
+    if (prof) {
+        std::vector<tt_lazy::OpProfile> p;
+        for (size_t i = 0; i < marks.size(); ++i) {
+            float ms = 0.0f;
+            if (ttc_timer_elapsed(marks[i].first, marks[i].second, &ms) != TTC_OK)
+                throw std::runtime_error(ttc_last_error());
+            p.push_back({labels[i], (double)ms});
+        }
+        tt_lazy::g_last_profile = std::move(p);
     }
 }
 
@@ -1160,6 +1208,12 @@ void CompiledTape::capture() {
     const auto mm0 = mm.stats();
     ttc_memory_stats before;
     ttc_get_memory_stats(&before);
+    const bool prof = profiling();
+    set_profiling(false);  // event waits cannot be recorded into a graph
+    struct Restore {
+        bool on;
+        ~Restore() { set_profiling(on); }
+    } restore{prof};
     check(ttc_capture_begin());
     void* exec = nullptr;
     try {

@@ -48,6 +48,20 @@ void register_all_operations(TapeExecutor& executor);
 
 namespace tt_lazy {
 
+// Tracing: while profiling is on (set_profiling, or TT_LAZY_PROFILE=1), every
+// tape operation runs inside an NVTX range named after it and between two
+// CUDA-event marks; last_profile() holds the device time of each operation
+// of the most recent tape execution (evaluate or Plan.run), in tape order.
+struct OpProfile {
+    std::string op;
+    double ms = 0.0;
+};
+void set_profiling(bool on);
+bool profiling();
+std::vector<OpProfile> last_profile();
+// "FusedGemm[matmul -> relu]", "FusedChain[...]" or the graph op's name.
+std::string op_label(const TapeOperation& op);
+
 // Selects the GPU (TT_LAZY_DEVICE, else LOCAL_RANK, else 0) and initialises
 // the CUDA backend once. Throws std::runtime_error when no B200 is present.
 void backend_init();

@@ -184,6 +184,18 @@ PYBIND11_MODULE(_tt_lazy, m) {
         return d;
     });
     m.def("reset_peak", []() { tt_lazy::MemoryManager::instance().reset_peak(); });
+    m.def("set_profiling", &tt_lazy::set_profiling,
+          "time every tape operation with CUDA events (and mark it with an NVTX range)");
+    m.def("profile", []() {
+        py::list out;
+        for (const auto& p : tt_lazy::last_profile()) {
+            py::dict d;
+            d["op"] = p.op;
+            d["ms"] = p.ms;
+            out.append(d);
+        }
+        return out;
+    });
     m.def("set_gemm_path", [](const std::string& p) {
         tt_lazy::set_gemm_path(p == "ffma" ? TTC_GEMM_FFMA : p == "tf32" ? TTC_GEMM_TF32 : TTC_GEMM_AUTO);
     });
