@@ -428,3 +428,49 @@ def test_profiling_times_every_tape_operation():
     plan.capture()  # recording turns the marks off by itself
     plan.run()
     assert tl.profile() == prof or len(tl.profile()) == len(prof)
+
+
+def test_guard_bands_find_no_overrun_and_catch_a_planted_one():
+    """Canary mode: every device buffer carries a 256-byte guard band that is
+    read back after each tape operation. The hot-path graphs (chains with
+    ragged shapes, segmented chains over transposed views, TF32 / FFMA GEMMs
+    with epilogue column sums, densified rank-3 views) leave every band
+    intact; a band overwritten on purpose (an in-bounds host write into the
+    band itself) is reported."""
+    from tt_lazy_b200 import capi
+
+    tl.set_canaries(True)
+    try:
+        rng = np.random.default_rng(44)
+        x = rng.uniform(-1, 1, (999, 1001)).astype(np.float32)
+        X = tl.constant(x)
+        w = tl.multiply(tl.add(tl.relu(X), X), tl.sigmoid(X))
+        tl.evaluate([w, tl.reduce_sum(w, [0]), tl.reduce_mean(w, [1])])
+        a = rng.uniform(-1, 1, (192, 160)).astype(np.float32)
+        outs = [tl.reduce_sum(tl.multiply(tl.sigmoid(c), tl.relu(tl.add(c, c))), [1])
+                for c in tl.split(tl.transpose(tl.constant(a)), 48, 1)]
+        tl.evaluate(outs)
+        for path in ("tf32", "ffma"):
+            tl.set_gemm_path(path)
+            m = rng.standard_normal((520, 64)).astype(np.float32)
+            k = (rng.standard_normal((64, 1032)) / 8).astype(np.float32)
+            tl.evaluate([tl.reduce_sum(tl.sigmoid(tl.matmul(tl.constant(m), tl.constant(k))), [0])])
+        r3 = rng.uniform(-1, 1, (4, 12, 8)).astype(np.float32)
+        tl.evaluate([tl.relu(ch) for ch in tl.split(tl.transpose(tl.constant(r3)), 5, 2)])
+        assert tl.check_canaries() == []
+        # planted: overwrite a live result's guard band from the host
+        plan = tl.Plan([tl.relu(tl.constant(x))])
+        plan.run()
+        ptr = plan.device_ptr(0)
+        off = tl.canary_offset(ptr)
+        assert off >= x.nbytes
+        junk = np.zeros(64, np.float32)
+        capi.check(capi.lib().ttc_memcpy_h2d(capi.C.c_void_p(ptr + off), junk.ctypes.data_as(capi.C.c_void_p), 256))
+        bad = tl.check_canaries()
+        assert len(bad) == 1 and "overwritten" in bad[0]
+        band = np.frombuffer(bytes(0xA5 ^ i for i in range(256)), np.uint8).copy()  # put the band back
+        capi.check(capi.lib().ttc_memcpy_h2d(capi.C.c_void_p(ptr + off), band.ctypes.data_as(capi.C.c_void_p), 256))
+        assert tl.check_canaries() == []
+    finally:
+        tl.set_canaries(False)
+        tl.set_gemm_path("auto")

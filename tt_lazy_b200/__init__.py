@@ -50,3 +50,6 @@ Plan = _fe.Plan
 stream = _fe.stream
 set_profiling = _fe.set_profiling
 profile = _fe.profile
+set_canaries = _fe.set_canaries
+check_canaries = _fe.check_canaries
+canary_offset = _fe.canary_offset

@@ -70,9 +70,52 @@ static size_t bucket(size_t bytes) {
     return (bytes + (2u << 20) - 1) & ~((size_t)(2u << 20) - 1);
 }
 
+namespace {
+// 256-byte guard pattern written after a buffer in canary mode
+const unsigned char* canary_pattern() {
+    static unsigned char p[256];
+    static bool init = [] {
+        for (int i = 0; i < 256; ++i) p[i] = (unsigned char)(0xA5 ^ i);
+        return true;
+    }();
+    (void)init;
+    return p;
+}
+}  // namespace
+
+bool MemoryManager::canaries() {
+    if (canaries_ < 0) {
+        const char* e = getenv("TT_LAZY_CANARY");
+        canaries_ = (e && e[0] == '1') ? 1 : 0;
+    }
+    return canaries_ == 1;
+}
+
+bool MemoryManager::band_intact(float* ptr, size_t bytes) {
+    unsigned char h[256];
+    if (ttc_memcpy_d2h(h, (const char*)ptr + bytes - 256, 256) != TTC_OK) return false;
+    return std::memcmp(h, canary_pattern(), 256) == 0;
+}
+
+std::vector<std::string> MemoryManager::check_canaries(const std::string& where) {
+    std::vector<std::string> out = std::move(violations_);
+    violations_.clear();
+    for (const auto& [ptr, bytes] : guarded_)
+        if (!band_intact(ptr, bytes))
+            out.push_back("guard band of the " + std::to_string(bytes - 256) + "-byte buffer at " +
+                          std::to_string((uintptr_t)ptr) + " overwritten (" + where + ")");
+    return out;
+}
+
+long long MemoryManager::canary_offset(const float* ptr) const {
+    auto it = guarded_.find(const_cast<float*>(ptr));
+    return it == guarded_.end() ? -1 : (long long)it->second - 256;
+}
+
 std::shared_ptr<DeviceBuffer> MemoryManager::allocate(size_t bytes) {
     backend_init();
-    const size_t b = bucket(std::max<size_t>(bytes, 4));
+    const bool guard = canaries();
+    const size_t b = bucket(std::max<size_t>(bytes, 4) + (guard ? 256 : 0));
     float* p = nullptr;
     auto& fl = free_[b];
     if (!fl.empty()) {
@@ -92,6 +135,12 @@ std::shared_ptr<DeviceBuffer> MemoryManager::allocate(size_t bytes) {
     stats_.bytes_live += b;
     stats_.bytes_peak = std::max(stats_.bytes_peak, stats_.bytes_live);
     if (recording_) recorded_.emplace_back(p, b);
+    if (guard) {  // the band is the bucket's last 256 bytes: past every request of this bucket
+        check(ttc_memcpy_h2d((char*)p + b - 256, canary_pattern(), 256));
+        guarded_[p] = b;
+    } else {
+        guarded_.erase(p);
+    }
     return std::make_shared<DeviceBuffer>(p, b);
 }
 
@@ -109,6 +158,13 @@ std::shared_ptr<DeviceBuffer> MemoryManager::claim(float* ptr, size_t bytes) {
 
 void MemoryManager::release(float* ptr, size_t bytes) {
     if (!ptr) return;
+    auto g = guarded_.find(ptr);
+    if (g != guarded_.end()) {  // (runs from a destructor: report later, never throw)
+        if (!band_intact(ptr, bytes))
+            violations_.push_back("guard band of a released " + std::to_string(bytes - 256) +
+                                  "-byte buffer overwritten");
+        guarded_.erase(g);
+    }
     free_[bytes].push_back(ptr);
     stats_.bytes_live -= bytes;
     stats_.bytes_cached += bytes;
@@ -280,6 +336,10 @@ void TapeExecutor::execute_tape(Tape& tape) {
         if (prof) {
             ttc_range_pop();
             if (ttc_timer_mark(&marks.back().second) != TTC_OK) throw std::runtime_error(ttc_last_error());
+        }
+        if (tt_lazy::MemoryManager::instance().canaries()) {
+            const auto bad = tt_lazy::MemoryManager::instance().check_canaries("after " + tt_lazy::op_label(*ops[i]));
+            if (!bad.empty()) throw std::runtime_error("tt_lazy: " + bad.front());
         }
         // release operands whose last reader just ran
         for (const auto& o : ops[i]->operands) {
@@ -1208,12 +1268,16 @@ void CompiledTape::capture() {
     const auto mm0 = mm.stats();
     ttc_memory_stats before;
     ttc_get_memory_stats(&before);
-    const bool prof = profiling();
-    set_profiling(false);  // event waits cannot be recorded into a graph
+    const bool prof = profiling(), guard = MemoryManager::instance().canaries();
+    set_profiling(false);  // event waits and guard-band reads cannot be recorded into a graph
+    MemoryManager::instance().set_canaries(false);
     struct Restore {
-        bool on;
-        ~Restore() { set_profiling(on); }
-    } restore{prof};
+        bool prof, guard;
+        ~Restore() {
+            set_profiling(prof);
+            MemoryManager::instance().set_canaries(guard);
+        }
+    } restore{prof, guard};
     check(ttc_capture_begin());
     void* exec = nullptr;
     try {

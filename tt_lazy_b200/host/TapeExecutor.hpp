@@ -6,6 +6,7 @@
 #include <map>
 #include <memory>
 #include <unordered_map>
+#include <string>
 #include <vector>
 
 #include "Tape.hpp"
@@ -122,11 +123,25 @@ class MemoryManager {
     }
     std::shared_ptr<DeviceBuffer> claim(float* ptr, size_t bytes);
 
+    // Guard bands (debug; set_canaries(true) or TT_LAZY_CANARY=1): each
+    // buffer gets 256 extra bytes at its end filled with a known pattern;
+    // check_canaries() reads every live band back (and release() each freed
+    // one) and reports the buffers whose band was written, i.e. an overrun.
+    void set_canaries(bool on) { canaries_ = on ? 1 : 0; }
+    bool canaries();
+    std::vector<std::string> check_canaries(const std::string& where);
+    // Byte offset of `ptr`'s guard band (-1 when it has none).
+    long long canary_offset(const float* ptr) const;
+
    private:
     std::unordered_map<size_t, std::vector<float*>> free_;
     Stats stats_;
     bool recording_ = false;
     std::vector<std::pair<float*, size_t>> recorded_;
+    int canaries_ = -1;                          // -1: from TT_LAZY_CANARY on first use
+    std::unordered_map<float*, size_t> guarded_;  // live buffers with a band -> bytes
+    std::vector<std::string> violations_;        // found at release, reported by check_canaries
+    bool band_intact(float* ptr, size_t bytes);
 };
 
 // Device copies of constant tensors (host pointer + size -> device buffer),

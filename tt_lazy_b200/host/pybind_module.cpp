@@ -184,6 +184,12 @@ PYBIND11_MODULE(_tt_lazy, m) {
         return d;
     });
     m.def("reset_peak", []() { tt_lazy::MemoryManager::instance().reset_peak(); });
+    m.def("set_canaries", [](bool on) { tt_lazy::MemoryManager::instance().set_canaries(on); },
+          "guard bands after every device buffer, checked after each tape operation (debug)");
+    m.def("check_canaries", []() { return tt_lazy::MemoryManager::instance().check_canaries("on request"); });
+    m.def("canary_offset", [](uintptr_t ptr) {
+        return tt_lazy::MemoryManager::instance().canary_offset(reinterpret_cast<const float*>(ptr));
+    });
     m.def("set_profiling", &tt_lazy::set_profiling,
           "time every tape operation with CUDA events (and mark it with an NVTX range)");
     m.def("profile", []() {
