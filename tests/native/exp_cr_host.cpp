@@ -1,7 +1,7 @@
 // Host build of tt_lazy_b200/csrc/exp_cr.cuh (the device exp of the sigmoid
 // step) with each CUDA intrinsic mapped to the IEEE operation it names, so
-// the float-float method can be checked against a long-double exp over a
-// large sweep of floats on the CPU. Compile with -ffp-contract=off: every
+// table method can be checked against a long-double exp over a large sweep
+// of floats on the CPU. Compile with -ffp-contract=off: every
 // intrinsic below is one correctly rounded operation, as on the device.
 //
 // usage: exp_cr_host STRIDE  -> prints "n=<count> mismatches=<m> over1ulp=<k>"
@@ -46,6 +46,20 @@ static inline double __longlong_as_double(long long i) {
     return d;
 }
 static inline float __double2float_rn(double d) { return (float)d; }
+static inline int __double2loint(double d) {
+    unsigned long long u;
+    std::memcpy(&u, &d, 8);
+    return (int)(unsigned)u;
+}
+// fma rounded toward -inf, in the one form the header uses: S + floor(a * b)
+// for a shifter S = 1.5 * 2^52 (the sum's ulp is 1), with the product exact.
+static inline double __fma_rd(double a, double b, double S) {
+    const double p = a * b;
+    const double e = std::fma(a, b, -p);  // a * b = p + e exactly
+    double f = std::floor(p);
+    if (f == p && e < 0) f -= 1.0;
+    return S + f;
+}
 static inline int __float2int_rn(float f) { return (int)std::lrintf(f); }
 using std::exp2;
 
