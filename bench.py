@@ -235,6 +235,98 @@ def run_reference(args):
 
 
 # ------------------------------------------------------------------ our arm
+def _device_ms(torch, stream, fn, reps):
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def other_configs(torch, tl, stream, hbm_peak, tf32_peak):
+    """README chain (1000^2 as configured, and 16384^2 for the HBM figure),
+    the small MLP and the DAG stress graph, each through tl.Plan; the small
+    ones also as captured CUDA graphs (launch-bound at their sizes)."""
+    from tt_lazy_b200 import workloads
+
+    out, launches = {}, 0
+
+    def plan_times(outs, reps, capture=True):
+        nonlocal launches
+        plan = tl.Plan(outs)
+        for _ in range(3):
+            plan.run()
+        ms = _device_ms(torch, stream, plan.run, reps)
+        launches += plan.kernels_last_run * (reps + 3)
+        res = {"ms": ms, "kernels_per_run": plan.kernels_last_run, "tape_ops": len(plan)}
+        if capture:
+            plan.capture()
+            for _ in range(3):
+                plan.run()
+            res["ms_graph"] = _device_ms(torch, stream, plan.run, reps)
+            launches += plan.kernels_last_run * (reps + 3)
+        return plan, res
+
+    # README chain
+    w, s, work = workloads.readme_chain(1000)
+    plan, r = plan_times([w, s], 200)
+    out["readme_chain_1000"] = {
+        "workload": "x[1000,1000] U(-1,1) seed 0: w = (relu(x) + relu(x))^2, s = sum(w); outputs w and s",
+        "bytes": work["bytes"], "us_per_run": r["ms"] * 1e3, "us_per_run_graph": r["ms_graph"] * 1e3,
+        "GBs_graph": work["bytes"] / (r["ms_graph"] * 1e-3) / 1e9, "kernels_per_run": r["kernels_per_run"],
+        "note": "8 MB fits in L2: launch-bound"}
+    del plan, w, s
+    w, s, work = workloads.readme_chain(16384)
+    plan, r = plan_times([w, s], 20, capture=False)
+    gbs = work["bytes"] / (r["ms"] * 1e-3) / 1e9
+    out["readme_chain_16384"] = {
+        "workload": "the same chain on x[16384,16384] (2 GiB moved per run)", "bytes": work["bytes"],
+        "ms_per_run": r["ms"], "GBs": gbs, "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm_peak,
+                                                        "unit": "GB/s", "frac": gbs / hbm_peak},
+        "kernels_per_run": r["kernels_per_run"]}
+    del plan, w, s
+    tl.clear_cache()
+    # small MLP
+    m, work = workloads.small_mlp()
+    plan, r = plan_times([m], 200)
+    out["small_mlp"] = {
+        "workload": "X[256,512] N(0,1), W1[512,1024], W2[1024,512] N(0,1/fan_in), b U(-0.1,0.1), seed 1: "
+                    "reduce_mean(relu(X W1 + b1) W2 + b2, dim 0)",
+        "flops": work["flops"], "us_per_run": r["ms"] * 1e3, "us_per_run_graph": r["ms_graph"] * 1e3,
+        "TFLOPs_graph": work["flops"] / (r["ms_graph"] * 1e-3) / 1e12, "kernels_per_run": r["kernels_per_run"],
+        "tape_ops": r["tape_ops"], "note": "0.5 GFLOP: launch- and latency-bound"}
+    del plan, m
+    tl.clear_cache()
+    # DAG stress
+    t0 = time.perf_counter()
+    outs, work = workloads.dag_stress()
+    t1 = time.perf_counter()
+    plan = tl.Plan(outs)
+    t2 = time.perf_counter()
+    plan.run()
+    torch.cuda.synchronize()
+    t3 = time.perf_counter()
+    for _ in range(2):
+        plan.run()
+    ms = _device_ms(torch, stream, plan.run, 5)
+    launches += plan.kernels_last_run * 8
+    out["dag_stress"] = {
+        "workload": f"random DAG seed 4: {work['graph_nodes']} nodes over [4096,4096] "
+                    f"({work['dead_ops']} unreachable), ops {work['counts']}, reduce_sum(dim 1) at 4 sinks",
+        "graph_build_ms": (t1 - t0) * 1e3, "tape_build_ms": (t2 - t1) * 1e3, "first_eval_ms": (t3 - t2) * 1e3,
+        "eval_ms": ms, "tape_ops": len(plan), "kernels_per_run": plan.kernels_last_run,
+        "live_ops": work["live_ops"], "flops": work["flops"], "bytes_unfused": work["bytes_unfused"],
+        "TFLOPs": work["flops"] / (ms * 1e-3) / 1e12,
+        "matmul_roofline_frac": (work["flops"] / (ms * 1e-3) / 1e12) / tf32_peak}
+    del plan, outs
+    tl.clear_cache()
+    out["_launches"] = launches
+    return out
+
+
 def run_ours(args):
     import torch
 
@@ -407,6 +499,13 @@ def run_ours(args):
                               "frac": per_gpu / hbm_peak, "peak_source": peak_kind}}
         del cplan, outs
 
+    # ---- the other workloads (README chain, small MLP, DAG stress): replicas
+    # only, so rank 0 at N = 1 times them
+    others = None
+    if rank == 0 and world == 1 and not args.skip_configs:
+        others = other_configs(torch, tl, stream, hbm_peak, tf32_peak)
+        launches += others.pop("_launches")
+
     # ---- CPU baseline (rank 0, N = 1 only)
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu:
@@ -442,6 +541,7 @@ def run_ours(args):
                          "cta_pair_kernel": {"achieved": 2 * Mg * N1 * K1 / (pair_ms * 1e-3) / 1e12,
                                              "launch_ms": pair_ms, "enabled_by": "TTC_GEMM_PAIR=1"}},
             "eltwise_chain": chain,
+            "other_configs": others,
             "cpu_baseline": cpu,
             "gpu_launches": int(launches),
             "clocks": clocks,
@@ -461,6 +561,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--skip-chain", action="store_true")
     ap.add_argument("--skip-cpu", action="store_true")
+    ap.add_argument("--skip-configs", action="store_true")
     ap.add_argument("--ref-seconds", type=float, default=12.0)
     args = ap.parse_args()
     if args.warmup < 3:

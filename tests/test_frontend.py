@@ -179,3 +179,27 @@ def test_pipelined_plan_rejects_graphs_that_are_not_row_local():
         tl.Plan([tl.reduce_sum(tl.relu(c((8, 8))), [0])], pipeline_chunks=2)
     with pytest.raises(RuntimeError, match="chunks must be"):
         tl.Plan([tl.reduce_sum(tl.relu(xs), [0])], pipeline_chunks=65)
+
+
+def test_dag_stress_workload_drops_dead_operations_and_fuses():
+    """The DCE / fusion stress graph (bench.py's dag_stress at a small size):
+    no unreachable operation reaches the tape, and fusion leaves fewer tape
+    operations than live graph operations."""
+    from tt_lazy_b200 import workloads
+
+    outs, work = workloads.dag_stress(n=32, nodes=200)
+    assert work["dead_ops"] == 80 and work["graph_nodes"] == 204
+    t = tl.tape(outs)
+    taped = set()
+    for op in t:
+        taped.add(op["node"])
+        taped.update(op["outputs"])
+    assert sum(op["fused_nodes"] for op in t) <= work["live_ops"]
+    assert len(t) < work["live_ops"]
+    # every taped node is an ancestor of an output: nothing from the dead part
+    produced = set()
+    for op in t:
+        for i in op["inputs"]:
+            assert i in produced or i not in taped
+        produced.update(op["outputs"])
+        produced.add(op["node"])

@@ -306,6 +306,23 @@ def test_gemm_tf32(ttc, m, k, n, ta, tb):
     assert err <= RTOL_TF32, err
 
 
+@pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (256, 1024, 512), (200, 1000, 520), (128, 4096, 256)])
+@pytest.mark.parametrize("act", ["relu", "sigmoid"])
+def test_gemm_tf32_split_k(ttc, m, k, n, act, monkeypatch):
+    """GEMMs with fewer output tiles than half the SMs split K over up to 16
+    work items (raw partial tiles, then a fixed-order sum and the epilogue in
+    a second kernel): the same bound against the oracle, close to the unsplit
+    kernel, and bit-identical from run to run."""
+    rng = np.random.default_rng(15)
+    got, want, _ = _gemm_case(ttc, m, k, n, 0, 0, ttc.GEMM_TF32, rng, act=act, bias=True)
+    assert normwise(got, want) <= RTOL_TF32
+    again, _, _ = _gemm_case(ttc, m, k, n, 0, 0, ttc.GEMM_TF32, np.random.default_rng(15), act=act, bias=True)
+    assert np.array_equal(got, again)
+    monkeypatch.setenv("TTC_GEMM_SPLITK", "0")
+    whole, _, _ = _gemm_case(ttc, m, k, n, 0, 0, ttc.GEMM_TF32, np.random.default_rng(15), act=act, bias=True)
+    assert normwise(got, whole) <= RTOL_TF32
+
+
 @pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (384, 100, 300), (1000, 260, 772), (520, 64, 1032),
                                    (1024, 512, 1280)])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
@@ -353,7 +370,7 @@ def test_invalid_descriptors_are_errors(ttc):
 
 
 @pytest.mark.parametrize("path", ["ffma", "tf32", "tf32_pair"])
-@pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (1000, 260, 772), (520, 64, 1032)])
+@pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (1000, 260, 772), (520, 64, 1032), (200, 1000, 520)])
 @pytest.mark.parametrize("mean,store", [(False, False), (True, True)])
 def test_gemm_epilogue_column_sum(ttc, path, m, k, n, mean, store, monkeypatch):
     """Epilogue reduction TTC_REDUCE_COLS: the column sums (or means) over the

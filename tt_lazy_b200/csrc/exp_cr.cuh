@@ -336,7 +336,8 @@ static __device__ __noinline__ float exp_cr_slow(float x, const ExpCrTable& t) {
     if (x > 89.0f) return __int_as_float(0x7f800000);  // overflows to +inf
     if (x < -104.0f) return 0.0f;                      // below half the smallest subnormal
     int k;
-    double e = exp_cr_poly(x, k) * t.t[k & 1023];
+    const double pk = exp_cr_poly(x, k);  // sets k: a separate statement (operands of * are unsequenced)
+    double e = pk * t.t[k & 1023];
     e = __longlong_as_double(__double_as_longlong(e) + (long long)(k >> 10) * (1ll << 52));  // * 2^m
     return __double2float_rn(e);
 }

@@ -54,6 +54,13 @@ struct TcParams {
     int* status;
     DProgram epi;
     float* partials;  // column sums of the final epilogue value per 32-row group, or null
+    // Split-K (single-CTA kernel only): work item w is split w % splits of
+    // tile w / splits, covering k-blocks [kb_per_split * split, ...). Each
+    // split stores its raw accumulator tile into split_ws, row-major
+    // [splits][m_blocks * BM][n_blocks * BN]; a second kernel adds the splits
+    // in split order and runs the epilogue on the sum.
+    int splits, kb_per_split;
+    float* split_ws;
 };
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -178,7 +185,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int num_tiles = p.m_blocks * p.n_blocks;
+    const int num_work = p.m_blocks * p.n_blocks * p.splits;
     bool failed = false;
 
     if (warp == 0) {
@@ -188,10 +195,12 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             long long issued = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && !failed; tile += gridDim.x) {
+            for (int w = blockIdx.x; w < num_work && !failed; w += gridDim.x) {
+                const int tile = w / p.splits, kb0 = (w % p.splits) * p.kb_per_split;
+                const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
                 int mb, nb;
                 tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(empty_bar(stage), phase ^ 1)) {
                         failed = true;
                         break;
@@ -244,7 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             int t = 0;
-            for (int tile = blockIdx.x; tile < num_tiles && !failed; tile += gridDim.x, ++t) {
+            for (int w = blockIdx.x; w < num_work && !failed; w += gridDim.x, ++t) {
+                const int kb0 = (w % p.splits) * p.kb_per_split;
+                const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
                 const int b = t & 1;
                 const uint32_t acc_phase = (t >> 1) & 1;
                 if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
@@ -253,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
-                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase)) {
                         failed = true;
                         break;
@@ -264,7 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                     for (int k = 0; k < BK / 8; ++k) {
                         const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, b_sbo, b_lay);
-                        tc_mma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+                        tc_mma_tf32(d_tmem, ad, bd, p.idesc, (kb != kb0 || k != 0) ? 1u : 0u);
                     }
                     tc_commit(empty_bar(stage));
                     if (++stage == STAGES) {
@@ -278,48 +289,82 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
         }
     } else {
         const int q = warp & 3;  // this warp's quarter of the 128 TMEM lanes
+        // Bias / activation / stores / column sums of one 32-column slice of
+        // this lane's row, from the tile's final values v32.
+        auto finish = [&](int mb, int nb, int c, const float (&v32)[32]) {
+            const long long row = (long long)mb * BM + q * 32 + lane;
+            const long long col0 = (long long)nb * BN + c * 32;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float v[4][4];
+                long long rr[4], cc[4];
+                bool vv[4];
+#pragma unroll
+                for (int g = 0; g < 4; ++g) {
+                    rr[g] = row;
+                    cc[g] = col0 + h * 16 + g * 4;
+                    vv[g] = row < p.M && cc[g] < p.N;
+#pragma unroll
+                    for (int w = 0; w < 4; ++w) v[g][w] = v32[h * 16 + g * 4 + w];
+                }
+                run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
+                if (p.partials) {
+#pragma unroll
+                    for (int g = 0; g < 4; ++g)
+#pragma unroll
+                        for (int w = 0; w < 4; ++w) v[g][w] = vv[g] ? v[g][w] : 0.0f;
+                    const long long rg = (long long)mb * (BM / 32) + q;
+                    warp_col_sums16(v, p.partials + rg * p.N + col0 + h * 16, lane, p.N - (col0 + h * 16));
+                }
+            }
+        };
         int t = 0;
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+        for (int wi = blockIdx.x; wi < num_work; wi += gridDim.x, ++t) {
+            const int tile = wi / p.splits, split = wi % p.splits;
             int mb, nb;
             tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
             const int b = t & 1;
             const uint32_t acc_phase = (t >> 1) & 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase));
+            if (p.splits == 1) {
+                if (!ok) {
+                    failed = true;
+                    break;
+                }
+                tc_fence_after();
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), r);
+                    tc_wait_ld();
+                    if ((long long)nb * BN + c * 32 >= p.N) continue;
+                    float v32[32];
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v32[j] = __uint_as_float(r[j]);
+                    finish(mb, nb, c, v32);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(tempty_bar(b));
+                continue;
+            }
+            // Split-K: store this split's raw tile and release the accumulator.
             if (!ok) {
                 failed = true;
                 break;
             }
             tc_fence_after();
-            const long long row = (long long)mb * BM + q * 32 + lane;
+            const long long ld = (long long)p.n_blocks * BN;
+            float* const dst = p.split_ws + ((long long)split * p.m_blocks * BM + (long long)mb * BM + q * 32 + lane) * ld +
+                               (long long)nb * BN;
             for (int c = 0; c < BN / 32; ++c) {
                 uint32_t r[32];
                 tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), r);
                 tc_wait_ld();
-                const long long col0 = (long long)nb * BN + c * 32;
-                if (col0 >= p.N) continue;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    float v[4][4];
-                    long long rr[4], cc[4];
-                    bool vv[4];
-#pragma unroll
-                    for (int g = 0; g < 4; ++g) {
-                        rr[g] = row;
-                        cc[g] = col0 + h * 16 + g * 4;
-                        vv[g] = row < p.M && cc[g] < p.N;
-#pragma unroll
-                        for (int w = 0; w < 4; ++w) v[g][w] = __uint_as_float(r[h * 16 + g * 4 + w]);
-                    }
-                    run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
-                    if (p.partials) {
-#pragma unroll
-                        for (int g = 0; g < 4; ++g)
-#pragma unroll
-                            for (int w = 0; w < 4; ++w) v[g][w] = vv[g] ? v[g][w] : 0.0f;
-                        const long long rg = (long long)mb * (BM / 32) + q;
-                        warp_col_sums16(v, p.partials + rg * p.N + col0 + h * 16, lane, p.N - (col0 + h * 16));
-                    }
-                }
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(dst + c * 32 + j) =
+                        make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                    __uint_as_float(r[j + 3]));
             }
             tc_fence_before();
             __syncwarp();
@@ -334,6 +379,65 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
     if (warp == 1)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
                      : "memory");
+}
+
+// Split-K epilogue: one warp per (32-row group, 16-column group), lane = row.
+// Adds the splits in split order (deterministic), then runs the epilogue
+// program and, for a fused column sum, writes the same per-32-row-group
+// partials as the GEMM epilogue (every group of the padded row range, rows
+// past M contributing zeros).
+struct SplitEpiParams {
+    const float* ws;
+    long long ld, split_stride;  // row stride of a split, elements between splits
+    int splits, M, N;
+    long long row_groups;        // padded rows / 32
+    DProgram epi;
+    float* partials;
+};
+
+__global__ void __launch_bounds__(256) splitk_epilogue_kernel(const __grid_constant__ SplitEpiParams p) {
+    if (p.epi.has_sigmoid) exp2_table_init_block();
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int cgroups = (p.N + 15) / 16;
+    const long long warp_id = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (warp_id >= p.row_groups * cgroups) return;  // whole warps only
+    const long long rg = warp_id / cgroups;
+    const long long col0 = (long long)(warp_id % cgroups) * 16;
+    const long long row = rg * 32 + lane;
+    const float* src = p.ws + row * p.ld + col0;
+    float v[4][4];
+    long long rr[4], cc[4];
+    bool vv[4];
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const float4 t = __ldcg(reinterpret_cast<const float4*>(src + 4 * g));
+        v[g][0] = t.x;
+        v[g][1] = t.y;
+        v[g][2] = t.z;
+        v[g][3] = t.w;
+        rr[g] = row;
+        cc[g] = col0 + 4 * g;
+        vv[g] = row < p.M && cc[g] < p.N;
+    }
+    for (int sp = 1; sp < p.splits; ++sp) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            const float4 t = __ldcg(reinterpret_cast<const float4*>(src + sp * p.split_stride + 4 * g));
+            v[g][0] += t.x;
+            v[g][1] += t.y;
+            v[g][2] += t.z;
+            v[g][3] += t.w;
+        }
+    }
+    run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
+    if (p.partials) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+#pragma unroll
+            for (int w = 0; w < 4; ++w) v[g][w] = vv[g] ? v[g][w] : 0.0f;
+        warp_col_sums16(v, p.partials + rg * p.N + col0, lane, p.N - col0);
+    }
 }
 
 // ------------------------------------------------------------------ pair MMA
@@ -701,6 +805,17 @@ int launch_pair(TcParams& p) {
     return TTC_OK;
 }
 
+// Split-K for GEMMs with too few output tiles to occupy the GPU (the small
+// MLP's 256 x 1024 x 512 is 8 tiles on 148 SMs): about one work item per SM,
+// at least 2 k-blocks (64 deep) per split, at most 16 splits. Off with
+// TTC_GEMM_SPLITK=0 (read at every call).
+int split_count(long long tiles, int k_blocks, int sms) {
+    const char* e = getenv("TTC_GEMM_SPLITK");
+    if ((e && e[0] == '0') || tiles * 2 > sms || k_blocks < 4) return 1;
+    const long long fill = (sms + tiles - 1) / tiles;
+    return (int)std::max<long long>(1, std::min<long long>(std::min<long long>(fill, k_blocks / 2), 16));
+}
+
 }  // namespace
 
 void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg, float* out, long long sseg, int mean,
@@ -750,20 +865,46 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
     const long long tiles = (long long)p.m_blocks * p.n_blocks;
     if (tiles > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many GEMM tiles");
     const long long groups = (long long)p.m_blocks * (tm / 32);  // every 32-row group of every row tile
-    if (reduce_out) {
-        if (groups > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many rows for the fused column sum");
+    if (reduce_out && groups > INT32_MAX)
+        return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many rows for the fused column sum");
+    p.splits = pair ? 1 : split_count(tiles, p.k_blocks, rt().sm_count);
+    p.kb_per_split = (p.k_blocks + p.splits - 1) / p.splits;
+    p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // every split has k-blocks
+    const size_t part_bytes = reduce_out ? ((size_t)groups * d.N * sizeof(float) + 255) & ~(size_t)255 : 0;
+    const long long mp = (long long)p.m_blocks * BM, np = (long long)p.n_blocks * BN;
+    const size_t split_bytes = p.splits > 1 ? (size_t)p.splits * mp * np * sizeof(float) : 0;
+    if (part_bytes + split_bytes) {
         void* ws = nullptr;
-        if (int rc = workspace((size_t)groups * d.N * sizeof(float), &ws)) return rc;
-        p.partials = (float*)ws;
+        if (int rc = workspace(part_bytes + split_bytes, &ws)) return rc;
+        if (reduce_out) p.partials = (float*)ws;
+        if (p.splits > 1) p.split_ws = (float*)((char*)ws + part_bytes);
     }
     if (pair) {
         if (int rc = launch_pair(p)) return rc;
         if (int rc = check_cuda(cudaGetLastError(), "TF32 pair GEMM launch")) return rc;
     } else {
-        const int grid = (int)(tiles < rt().sm_count ? tiles : rt().sm_count);
+        const long long work = tiles * p.splits;
+        const int grid = (int)(work < rt().sm_count ? work : rt().sm_count);
         tf32_gemm_kernel<<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
         count_launch();
         if (int rc = check_cuda(cudaGetLastError(), "TF32 GEMM launch")) return rc;
+        if (p.splits > 1) {
+            SplitEpiParams e;
+            std::memset(&e, 0, sizeof e);
+            e.ws = p.split_ws;
+            e.ld = np;
+            e.split_stride = mp * np;
+            e.splits = p.splits;
+            e.M = d.M;
+            e.N = d.N;
+            e.row_groups = mp / 32;
+            e.epi = epi;
+            e.partials = p.partials;
+            const long long warps = e.row_groups * ((d.N + 15) / 16);
+            splitk_epilogue_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, rt().stream>>>(e);
+            count_launch();
+            if (int rc = check_cuda(cudaGetLastError(), "split-K epilogue launch")) return rc;
+        }
     }
     if (reduce_out) {  // rows past M contribute exact zeros
         launch_finalize_cols(p.partials, (int)groups, d.N, 1, reduce_out, 0, mean, (double)d.M);

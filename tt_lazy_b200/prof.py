@@ -2,6 +2,7 @@
 
     python -m tt_lazy_b200.prof gemm [M]      # tf32_gemm_kernel: X[M,4096] . W[4096,16384], 3 launches
     python -m tt_lazy_b200.prof chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
+    python -m tt_lazy_b200.prof small_mlp      # the small MLP workload through tl.Plan, 3 runs
 
 NAME: copy | readme (relu -> add -> multiply, stored, summed) | sigmoid |
 segments (sigmoid(C) * relu(C + C) over 8 row segments, column sums).
@@ -65,7 +66,25 @@ def chain(name="segments", N=8192, reps=3):
     print(f"chain {name} {N}x{N} ok")
 
 
+def small_mlp(reps=3):
+    import torch
+
+    import tt_lazy_b200 as tl
+    from tt_lazy_b200 import workloads
+
+    tl.backend_init()
+    m, _ = workloads.small_mlp()
+    plan = tl.Plan([m])
+    for _ in range(reps):
+        plan.run()
+    torch.cuda.synchronize()
+    print(f"small_mlp ok, m[0] = {float(plan.numpy(0)[0]):.6g}, {plan.kernels_last_run} kernels per run")
+
+
 def main(argv):
+    if len(argv) >= 2 and argv[1] == "small_mlp":
+        small_mlp()
+        return 0
     if len(argv) < 2 or argv[1] not in ("gemm", "chain"):
         print(__doc__)
         return 2
