@@ -274,9 +274,16 @@ int ttc_copy2d(const float* in, int64_t in_ld, float* out, int64_t out_ld, int64
  *       TTC_GEMM_TF32 -- tcgen05.mma kind::tf32, TMEM accumulators, TMA
  *                         operand loads (the 2e-3 bound);
  *       TTC_GEMM_AUTO -- TF32 when the shape suits the tensor-core kernel,
- *                         else FFMA.
+ *                         else FFMA;
+ *       TTC_GEMM_TF32X3 -- fp32-accurate products on the tensor cores: each
+ *                         operand split into a TF32 part and a TF32 remainder
+ *                         (x = big + small), three kind::tf32 MMAs per step
+ *                         (big*big + big*small + small*big) into fp32 TMEM
+ *                         accumulators (the 1e-5 bound, ~1e-6 measured);
+ *                         shapes the tensor-core kernel does not take run on
+ *                         the FFMA path.
  */
-typedef enum { TTC_GEMM_AUTO = 0, TTC_GEMM_FFMA = 1, TTC_GEMM_TF32 = 2 } ttc_gemm_path;
+typedef enum { TTC_GEMM_AUTO = 0, TTC_GEMM_FFMA = 1, TTC_GEMM_TF32 = 2, TTC_GEMM_TF32X3 = 3 } ttc_gemm_path;
 
 typedef struct {
     int32_t M, N, K;
@@ -288,7 +295,7 @@ typedef struct {
 } ttc_gemm_desc;
 
 int ttc_gemm(const ttc_gemm_desc* desc);
-/* Which path ttc_gemm would take for this descriptor (TTC_GEMM_FFMA/TF32). */
+/* Which path ttc_gemm would take for this descriptor (TTC_GEMM_FFMA/TF32/TF32X3). */
 int ttc_gemm_select_path(const ttc_gemm_desc* desc);
 
 /* ------------------------------------------------ collective (multi-GPU)

@@ -203,3 +203,10 @@ def test_dag_stress_workload_drops_dead_operations_and_fuses():
             assert i in produced or i not in taped
         produced.update(op["outputs"])
         produced.add(op["node"])
+
+
+def test_gemm_path_names_are_checked():
+    with pytest.raises(ValueError, match="auto, ffma, tf32 or tf32x3"):
+        tl.set_gemm_path("fp64")
+    for p in ("ffma", "tf32", "tf32x3", "auto"):
+        tl.set_gemm_path(p)

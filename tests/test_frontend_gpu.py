@@ -66,7 +66,7 @@ def test_readme_chain_public_api(golden):
     assert np.array_equal(tl.multiply(zc, zc).numpy(), golden["chain_w"])
 
 
-@pytest.mark.parametrize("path,tol", [("ffma", 1e-5), ("tf32", 2e-3)])
+@pytest.mark.parametrize("path,tol", [("ffma", 1e-5), ("tf32", 2e-3), ("tf32x3", 1e-5)])
 def test_two_layer_mlp_mean(path, tol, golden):
     tl.set_gemm_path(path)
     rng = np.random.default_rng(1)

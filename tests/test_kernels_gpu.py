@@ -306,6 +306,35 @@ def test_gemm_tf32(ttc, m, k, n, ta, tb):
     assert err <= RTOL_TF32, err
 
 
+@pytest.mark.parametrize("m,k,n", [(128, 32, 128), (256, 512, 1024), (384, 100, 300), (1000, 260, 772),
+                                   (128, 4096, 256), (520, 64, 1032), (1024, 512, 1280)])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])
+def test_gemm_tf32x3(ttc, m, k, n, ta, tb):
+    """Three-pass TF32 (x = big + small, big*big + big*small + small*big on
+    the tensor cores): the FFMA path's 1e-5 bound."""
+    rng = np.random.default_rng(16)
+    got, want, g = _gemm_case(ttc, m, k, n, ta, tb, ttc.GEMM_TF32X3, rng, act="sigmoid", bias=True)
+    assert ttc.gemm_select_path(g) == ttc.GEMM_TF32X3
+    err = normwise(got, want)
+    assert err <= RTOL_FFMA, err
+
+
+def test_gemm_tf32x3_wide_range_and_small_shapes(ttc):
+    """Operands spanning many binades keep the 1e-5 bound (the remainder is
+    scaled with its element); shapes the tensor-core kernel does not take
+    run on the FFMA path."""
+    rng = np.random.default_rng(17)
+    a = (rng.standard_normal((256, 384)) * np.exp2(rng.integers(-20, 20, (256, 384)))).astype(np.float32)
+    b = (rng.standard_normal((384, 512)) * np.exp2(rng.integers(-20, 20, (384, 512)))).astype(np.float32)
+    A, B = dev(ttc, a), dev(ttc, b)
+    C = ttc.DeviceArray.empty((256, 512))
+    ttc.gemm(256, 512, 384, A.ptr, 384, B.ptr, 512, C.ptr, 512, path=ttc.GEMM_TF32X3)
+    assert normwise(C.numpy(), oracle.matmul(a, b)) <= RTOL_FFMA
+    got, want, g = _gemm_case(ttc, 45, 67, 29, 0, 0, ttc.GEMM_TF32X3, rng)
+    assert ttc.gemm_select_path(g) == ttc.GEMM_FFMA
+    assert normwise(got, want) <= RTOL_FFMA
+
+
 @pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (256, 1024, 512), (200, 1000, 520), (128, 4096, 256)])
 @pytest.mark.parametrize("act", ["relu", "sigmoid"])
 def test_gemm_tf32_split_k(ttc, m, k, n, act, monkeypatch):
@@ -369,7 +398,7 @@ def test_invalid_descriptors_are_errors(ttc):
         ttc.gemm(4, 4, 4, X.ptr, 2, X.ptr, 4, X.ptr, 4)
 
 
-@pytest.mark.parametrize("path", ["ffma", "tf32", "tf32_pair"])
+@pytest.mark.parametrize("path", ["ffma", "tf32", "tf32_pair", "tf32x3"])
 @pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (1000, 260, 772), (520, 64, 1032), (200, 1000, 520)])
 @pytest.mark.parametrize("mean,store", [(False, False), (True, True)])
 def test_gemm_epilogue_column_sum(ttc, path, m, k, n, mean, store, monkeypatch):
@@ -393,11 +422,11 @@ def test_gemm_epilogue_column_sum(ttc, path, m, k, n, mean, store, monkeypatch):
         outs = [ttc.out_view(C.ptr, n)]
     epi = ttc.chain_desc(m, n, [ttc.in_view(Bv.ptr, 0)], outs, prog, reduce=ttc.REDUCE_COLS, reduce_out=S.ptr,
                          mean=mean)
-    p = ttc.GEMM_FFMA if path == "ffma" else ttc.GEMM_TF32
+    p = {"ffma": ttc.GEMM_FFMA, "tf32x3": ttc.GEMM_TF32X3}.get(path, ttc.GEMM_TF32)
     ttc.gemm(m, n, k, A.ptr, k, B.ptr, n, path=p, epilogue=epi)
     y = oracle.sigmoid(oracle.add(oracle.matmul(a, b), bias))
     want = oracle.reduce(y, (0,), mean=mean, f64=True)
-    tol = RTOL_FFMA if path == "ffma" else RTOL_TF32
+    tol = RTOL_FFMA if path in ("ffma", "tf32x3") else RTOL_TF32
     assert normwise(S.numpy(), want) <= tol
     if store:
         assert normwise(C.numpy(), y) <= tol

@@ -27,7 +27,7 @@ SRC_ACC, SRC_INPUT, SRC_SLOT = range(3)
 # ttc_reduce_mode
 REDUCE_NONE, REDUCE_ALL, REDUCE_ROWS, REDUCE_COLS = range(4)
 # ttc_gemm_path
-GEMM_AUTO, GEMM_FFMA, GEMM_TF32 = range(3)
+GEMM_AUTO, GEMM_FFMA, GEMM_TF32, GEMM_TF32X3 = range(4)
 
 
 class Instr(C.Structure):

@@ -1,5 +1,6 @@
 // gemm_ffma.cu -- fp32 CUDA-core GEMM (the 1e-5 accuracy path) and the
-// ttc_gemm entry point that picks between it and the tcgen05 TF32 kernel.
+// ttc_gemm entry point that picks between it and the tcgen05 kernels (TF32,
+// and the fp32-accurate three-pass TF32X3).
 //
 // Replaces math::matmul (src/backend/cpu/matmul.cpp:36-85, an i-j-k loop with
 // a strided read of B, 0.82 GFLOP/s) and math::fused_mlp
@@ -19,7 +20,7 @@
 
 namespace ttc {
 
-int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean);
+int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean, bool x3);
 bool tf32_supported(const ttc_gemm_desc& d, const DProgram& epi, bool epi_vec);
 int run_chain(const ttc_chain_desc& d);
 
@@ -236,7 +237,8 @@ int ttc_gemm_select_path(const ttc_gemm_desc* desc) {
     if (make_epilogue(*desc, &e) != TTC_OK) return TTC_GEMM_FFMA;
     DProgram prog;
     if (decode_program(e, true, &prog) != TTC_OK) return TTC_GEMM_FFMA;
-    if (tf32_supported(*desc, prog, epilogue_vec_ok(e, desc->N))) return TTC_GEMM_TF32;
+    if (tf32_supported(*desc, prog, epilogue_vec_ok(e, desc->N)))
+        return desc->path == TTC_GEMM_TF32X3 ? TTC_GEMM_TF32X3 : TTC_GEMM_TF32;
     return TTC_GEMM_FFMA;
 }
 
@@ -269,7 +271,7 @@ int ttc_gemm(const ttc_gemm_desc* desc) {
     if (int rc = decode_program(e, true, &p.epi)) return rc;
     const bool vec = epilogue_vec_ok(e, d.N);
     if (d.path != TTC_GEMM_FFMA && tf32_supported(d, p.epi, vec))
-        return run_gemm_tf32(d, p.epi, reduce ? e.reduce_out : nullptr, e.reduce_mean);
+        return run_gemm_tf32(d, p.epi, reduce ? e.reduce_out : nullptr, e.reduce_mean, d.path == TTC_GEMM_TF32X3);
     if (reduce) {
         // FFMA path: the final epilogue value goes to a scratch matrix, then
         // one column-sum chain over it.

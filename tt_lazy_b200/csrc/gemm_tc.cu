@@ -39,14 +39,20 @@ constexpr int BM = 128, BN = 256, BK = 32, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 4;  // 16 KB
 constexpr int B_BYTES = BN * BK * 4;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int TMEM_COLS = 2 * BN;
 constexpr int kThreads = 192;
 constexpr int GROUP_M = 16;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+// TF32X3 variant: 128x128 output tiles, 3 stages of 64 KB (A and B, each as
+// its TF32 part and TF32 remainder), same shared memory footprint.
+constexpr int X3_BN = 128, X3_STAGES = 3;
+constexpr int X3_SMEM_BYTES = X3_STAGES * 2 * (A_BYTES + X3_BN * BK * 4) + 1024 + 256;
+static_assert(X3_SMEM_BYTES <= SMEM_BYTES, "TF32X3 stages exceed the kernel's shared memory");
 
 struct TcParams {
     CUtensorMap tma_a;
     CUtensorMap tma_b;
+    CUtensorMap tma_a2;  // TF32X3: the TF32 remainders of A and B (same geometry)
+    CUtensorMap tma_b2;
     int M, N, K;
     int m_blocks, n_blocks, k_blocks;
     int a_mn_major, b_mn_major;
@@ -150,21 +156,27 @@ __device__ __forceinline__ void tile_coords(int tile, int m_blocks, int n_blocks
     nb = local / gm;
 }
 
+template <bool X3>
 __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_constant__ TcParams p) {
+    // X3: 128x128 tiles, stages of [A big | B big | A small | B small].
+    constexpr int TBN = X3 ? X3_BN : BN, TSTAGES = X3 ? X3_STAGES : STAGES;
+    constexpr int TB_BYTES = TBN * BK * 4;
+    constexpr int TSTAGE = X3 ? 2 * (A_BYTES + TB_BYTES) : A_BYTES + TB_BYTES;
+    constexpr int TTMEM = 2 * TBN;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
-    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4);
+    uint64_t* bars = (uint64_t*)(smem + TSTAGES * TSTAGE);
+    uint32_t* tmem_slot = (uint32_t*)(bars + 2 * TSTAGES + 4);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t sbase = smem_u32(smem);
     const uint32_t bar0 = smem_u32(bars);
     auto full_bar = [&](int s) { return bar0 + 8u * s; };
-    auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
-    auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + b); };
-    auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * STAGES + 2 + b); };
+    auto empty_bar = [&](int s) { return bar0 + 8u * (TSTAGES + s); };
+    auto tfull_bar = [&](int b) { return bar0 + 8u * (2 * TSTAGES + b); };
+    auto tempty_bar = [&](int b) { return bar0 + 8u * (2 * TSTAGES + 2 + b); };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; ++s) {
+        for (int s = 0; s < TSTAGES; ++s) {
             mbar_init(full_bar(s), 1);
             mbar_init(empty_bar(s), 1);
         }
@@ -177,7 +189,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
     if (p.epi.has_sigmoid) exp2_table_init_block();
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
+                     "r"(TTMEM)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -205,8 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                         failed = true;
                         break;
                     }
-                    mbar_arrive_expect_tx(full_bar(stage), STAGE_BYTES);
-                    const uint32_t a_dst = sbase + stage * STAGE_BYTES, b_dst = a_dst + A_BYTES;
+                    mbar_arrive_expect_tx(full_bar(stage), TSTAGE);
+                    const uint32_t a_dst = sbase + stage * TSTAGE, b_dst = a_dst + A_BYTES;
                     if (!p.a_mn_major) {
                         tma_load_2d(a_dst, &p.tma_a, full_bar(stage), kb * BK, mb * BM);
                     } else {
@@ -215,14 +227,33 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                             tma_load_2d(a_dst + j * (BK * 128), &p.tma_a, full_bar(stage), mb * BM + 32 * j, kb * BK);
                     }
                     if (!p.b_mn_major) {
-                        tma_load_2d(b_dst, &p.tma_b, full_bar(stage), kb * BK, nb * BN);
+                        tma_load_2d(b_dst, &p.tma_b, full_bar(stage), kb * BK, nb * TBN);
                     } else {
 #pragma unroll
-                        for (int j = 0; j < BN / 32; ++j)
-                            tma_load_2d(b_dst + j * (BK * 128), &p.tma_b, full_bar(stage), nb * BN + 32 * j, kb * BK);
+                        for (int j = 0; j < TBN / 32; ++j)
+                            tma_load_2d(b_dst + j * (BK * 128), &p.tma_b, full_bar(stage), nb * TBN + 32 * j, kb * BK);
+                    }
+                    if (X3) {  // the same boxes of the small parts
+                        const uint32_t a2_dst = b_dst + TB_BYTES, b2_dst = a2_dst + A_BYTES;
+                        if (!p.a_mn_major) {
+                            tma_load_2d(a2_dst, &p.tma_a2, full_bar(stage), kb * BK, mb * BM);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BM / 32; ++j)
+                                tma_load_2d(a2_dst + j * (BK * 128), &p.tma_a2, full_bar(stage), mb * BM + 32 * j,
+                                            kb * BK);
+                        }
+                        if (!p.b_mn_major) {
+                            tma_load_2d(b2_dst, &p.tma_b2, full_bar(stage), kb * BK, nb * TBN);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < TBN / 32; ++j)
+                                tma_load_2d(b2_dst + j * (BK * 128), &p.tma_b2, full_bar(stage), nb * TBN + 32 * j,
+                                            kb * BK);
+                        }
                     }
                     ++issued;
-                    if (++stage == STAGES) {
+                    if (++stage == TSTAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -230,11 +261,11 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             }
             // Never leave with loads in flight: wait (bounded) for the most
             // recent load of every stage to land.
-            const long long last = issued < STAGES ? issued : STAGES;
+            const long long last = issued < TSTAGES ? issued : TSTAGES;
             for (long long i = 0; i < last; ++i) {
                 const long long n = issued - 1 - i;
-                const int s = (int)(n % STAGES);
-                const uint32_t ph = (uint32_t)((n / STAGES) & 1);
+                const int s = (int)(n % TSTAGES);
+                const uint32_t ph = (uint32_t)((n / TSTAGES) & 1);
                 if (!mbar_wait(full_bar(s), ph)) failed = true;
             }
         }
@@ -263,22 +294,29 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                     break;
                 }
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + (uint32_t)(b * BN);
+                const uint32_t d_tmem = tmem_base + (uint32_t)(b * TBN);
                 for (int kb = kb0; kb < kb1; ++kb) {
                     if (!mbar_wait(full_bar(stage), phase)) {
                         failed = true;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_s = sbase + stage * STAGE_BYTES, b_s = a_s + A_BYTES;
+                    const uint32_t a_s = sbase + stage * TSTAGE, b_s = a_s + A_BYTES;
 #pragma unroll
                     for (int k = 0; k < BK / 8; ++k) {
                         const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, b_sbo, b_lay);
                         tc_mma_tf32(d_tmem, ad, bd, p.idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+                        if (X3) {  // + big * small + small * big
+                            const uint32_t a2_s = b_s + TB_BYTES, b2_s = a2_s + A_BYTES;
+                            const uint64_t ad2 = make_desc(a2_s + k * a_kstep, a_lbo, a_sbo, a_lay);
+                            const uint64_t bd2 = make_desc(b2_s + k * b_kstep, b_lbo, b_sbo, b_lay);
+                            tc_mma_tf32(d_tmem, ad, bd2, p.idesc, 1u);
+                            tc_mma_tf32(d_tmem, ad2, bd, p.idesc, 1u);
+                        }
                     }
                     tc_commit(empty_bar(stage));
-                    if (++stage == STAGES) {
+                    if (++stage == TSTAGES) {
                         stage = 0;
                         phase ^= 1;
                     }
@@ -293,7 +331,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
         // this lane's row, from the tile's final values v32.
         auto finish = [&](int mb, int nb, int c, const float (&v32)[32]) {
             const long long row = (long long)mb * BM + q * 32 + lane;
-            const long long col0 = (long long)nb * BN + c * 32;
+            const long long col0 = (long long)nb * TBN + c * 32;
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 float v[4][4];
@@ -332,11 +370,11 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                     break;
                 }
                 tc_fence_after();
-                for (int c = 0; c < BN / 32; ++c) {
+                for (int c = 0; c < TBN / 32; ++c) {
                     uint32_t r[32];
-                    tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), r);
+                    tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TBN + c * 32), r);
                     tc_wait_ld();
-                    if ((long long)nb * BN + c * 32 >= p.N) continue;
+                    if ((long long)nb * TBN + c * 32 >= p.N) continue;
                     float v32[32];
 #pragma unroll
                     for (int j = 0; j < 32; ++j) v32[j] = __uint_as_float(r[j]);
@@ -353,12 +391,12 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                 break;
             }
             tc_fence_after();
-            const long long ld = (long long)p.n_blocks * BN;
+            const long long ld = (long long)p.n_blocks * TBN;
             float* const dst = p.split_ws + ((long long)split * p.m_blocks * BM + (long long)mb * BM + q * 32 + lane) * ld +
-                               (long long)nb * BN;
-            for (int c = 0; c < BN / 32; ++c) {
+                               (long long)nb * TBN;
+            for (int c = 0; c < TBN / 32; ++c) {
                 uint32_t r[32];
-                tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c * 32), r);
+                tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TBN + c * 32), r);
                 tc_wait_ld();
 #pragma unroll
                 for (int j = 0; j < 32; j += 4)
@@ -377,7 +415,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TTMEM)
                      : "memory");
 }
 
@@ -738,6 +776,35 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
 // elements (row pitch ld elements), box {32, box_outer}, out-of-bounds reads
 // filled with zeros. K-major tiles use the 16-byte-chunk 128-byte swizzle;
 // MN-major tiles the 32-byte-chunk one (matching descriptor layout 1).
+// TF32X3 operand split. big = x rounded to TF32 (nearest, ties to even; a
+// rounding that would carry into the exponent's all-ones pattern truncates
+// instead), small = (x - big) rounded the same way, so x = big + small to
+// ~2^-22 relative and both parts pass the tensor core's TF32 reading
+// unchanged. Non-finite x: big = x, small = 0.
+__device__ __forceinline__ float tf32_rn(float x) {
+    const unsigned u = __float_as_uint(x);
+    if ((u & 0x7f800000u) == 0x7f800000u) return x;
+    const unsigned r = (u + 0xfffu + ((u >> 13) & 1u)) & 0xffffe000u;
+    return __uint_as_float((r & 0x7f800000u) == 0x7f800000u ? (u & 0xffffe000u) : r);
+}
+
+// Rows of a stored operand (rows x cols, leading dimension lds) into dense
+// big / small copies with leading dimension ldd; blocks stride over rows,
+// threads over columns (coalesced).
+__global__ void __launch_bounds__(256) tf32_split_kernel(const float* __restrict__ src, long long rows, long long cols,
+                                                         long long lds, float* __restrict__ big,
+                                                         float* __restrict__ small, long long ldd) {
+    for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
+        for (long long c = threadIdx.x; c < cols; c += blockDim.x) {
+            const float x = __ldg(src + r * lds + c);
+            const float b = tf32_rn(x);
+            const bool finite = (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u;
+            big[r * ldd + c] = b;
+            small[r * ldd + c] = finite ? tf32_rn(__fsub_rn(x, b)) : 0.0f;
+        }
+    }
+}
+
 int make_map(CUtensorMap* map, const float* ptr, long long inner, long long outer, long long ld, int box_outer,
              bool mn_major) {
     const unsigned long long dims[2] = {(unsigned long long)inner, (unsigned long long)outer};
@@ -824,34 +891,35 @@ void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg,
 // `reduce_out` (or null): column sums (mean with `mean`) of the final
 // epilogue value over the M rows, from per-32-row partial sums the epilogue
 // writes into the workspace and a fixed-order fp64 finalize.
-int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean) {
+int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean, bool x3) {
     static bool attr_set = false;
     if (!attr_set) {
-        TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      SMEM_BYTES));
+        TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      X3_SMEM_BYTES));
         attr_set = true;
     }
-    const bool pair = use_pair(d);
-    const int bn = pair ? P_BNH : BN;  // B columns one CTA loads per tile
+    const bool pair = !x3 && use_pair(d);
+    const int bn = pair ? P_BNH : x3 ? X3_BN : BN;  // B columns one CTA loads per tile
     TcParams p;
     std::memset(&p, 0, sizeof p);
     p.a_mn_major = d.trans_a ? 1 : 0;
     p.b_mn_major = d.trans_b ? 0 : 1;
-    // A: logical [M, K]; K-major when stored [M, K] (trans_a = 0).
-    if (!p.a_mn_major) {
-        if (int rc = make_map(&p.tma_a, d.a, d.K, d.M, d.lda, BM, false)) return rc;
-    } else {
-        if (int rc = make_map(&p.tma_a, d.a, d.M, d.K, d.lda, BK, true)) return rc;
-    }
-    // B: logical [K, N]; MN-major when stored [K, N] (trans_b = 0).
-    if (p.b_mn_major) {
-        if (int rc = make_map(&p.tma_b, d.b, d.N, d.K, d.ldb, BK, true)) return rc;
-    } else {
-        if (int rc = make_map(&p.tma_b, d.b, d.K, d.N, d.ldb, bn, false)) return rc;
-    }
+    // Stored operands: A is [M, K] ([K, M] when trans_a), B is [K, N] ([N, K]
+    // when trans_b). TF32X3 reads dense big / small copies of both.
+    const long long a_rows = d.trans_a ? d.K : d.M, a_cols = d.trans_a ? d.M : d.K;
+    const long long b_rows = d.trans_b ? d.N : d.K, b_cols = d.trans_b ? d.K : d.N;
+    const long long a_ld = x3 ? (a_cols + 3) & ~3ll : d.lda, b_ld = x3 ? (b_cols + 3) & ~3ll : d.ldb;
+    const size_t a_part = ((size_t)a_rows * a_ld * sizeof(float) + 255) & ~(size_t)255;
+    const size_t b_part = ((size_t)b_rows * b_ld * sizeof(float) + 255) & ~(size_t)255;
+    const size_t x3_bytes = x3 ? 2 * (a_part + b_part) : 0;
+    const float* a_ptr[2] = {d.a, nullptr};
+    const float* b_ptr[2] = {d.b, nullptr};
     p.M = d.M;
     p.N = d.N;
     p.K = d.K;
-    const int tm = pair ? 2 * BM : BM, tn = pair ? P_BN : BN;  // output tile of one CTA / CTA pair
+    const int tm = pair ? 2 * BM : BM, tn = pair ? P_BN : x3 ? X3_BN : BN;  // output tile of one CTA / CTA pair
     p.m_blocks = (d.M + tm - 1) / tm;
     p.n_blocks = (d.N + tn - 1) / tn;
     p.k_blocks = (d.K + BK - 1) / BK;
@@ -871,13 +939,46 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
     p.kb_per_split = (p.k_blocks + p.splits - 1) / p.splits;
     p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // every split has k-blocks
     const size_t part_bytes = reduce_out ? ((size_t)groups * d.N * sizeof(float) + 255) & ~(size_t)255 : 0;
-    const long long mp = (long long)p.m_blocks * BM, np = (long long)p.n_blocks * BN;
-    const size_t split_bytes = p.splits > 1 ? (size_t)p.splits * mp * np * sizeof(float) : 0;
-    if (part_bytes + split_bytes) {
+    const long long mp = (long long)p.m_blocks * BM, np = (long long)p.n_blocks * tn;
+    const size_t split_bytes = p.splits > 1 ? ((size_t)p.splits * mp * np * sizeof(float) + 255) & ~(size_t)255 : 0;
+    if (part_bytes + split_bytes + x3_bytes) {
         void* ws = nullptr;
-        if (int rc = workspace(part_bytes + split_bytes, &ws)) return rc;
+        if (int rc = workspace(part_bytes + split_bytes + x3_bytes, &ws)) return rc;
         if (reduce_out) p.partials = (float*)ws;
         if (p.splits > 1) p.split_ws = (float*)((char*)ws + part_bytes);
+        if (x3) {
+            char* x = (char*)ws + part_bytes + split_bytes;
+            float* parts[4] = {(float*)x, (float*)(x + a_part), (float*)(x + 2 * a_part),
+                               (float*)(x + 2 * a_part + b_part)};
+            const int sms = rt().sm_count;
+            tf32_split_kernel<<<(unsigned)std::min<long long>(a_rows, 8ll * sms), 256, 0, rt().stream>>>(
+                d.a, a_rows, a_cols, d.lda, parts[0], parts[1], a_ld);
+            count_launch();
+            tf32_split_kernel<<<(unsigned)std::min<long long>(b_rows, 8ll * sms), 256, 0, rt().stream>>>(
+                d.b, b_rows, b_cols, d.ldb, parts[2], parts[3], b_ld);
+            count_launch();
+            if (int rc = check_cuda(cudaGetLastError(), "TF32X3 operand split launch")) return rc;
+            a_ptr[0] = parts[0];
+            a_ptr[1] = parts[1];
+            b_ptr[0] = parts[2];
+            b_ptr[1] = parts[3];
+        }
+    }
+    // A: logical [M, K]; K-major when stored [M, K] (trans_a = 0).
+    // B: logical [K, N]; MN-major when stored [K, N] (trans_b = 0).
+    for (int h = 0; h < (x3 ? 2 : 1); ++h) {
+        CUtensorMap* ma = h ? &p.tma_a2 : &p.tma_a;
+        CUtensorMap* mb_ = h ? &p.tma_b2 : &p.tma_b;
+        if (!p.a_mn_major) {
+            if (int rc = make_map(ma, a_ptr[h], d.K, d.M, a_ld, BM, false)) return rc;
+        } else {
+            if (int rc = make_map(ma, a_ptr[h], d.M, d.K, a_ld, BK, true)) return rc;
+        }
+        if (p.b_mn_major) {
+            if (int rc = make_map(mb_, b_ptr[h], d.N, d.K, b_ld, BK, true)) return rc;
+        } else {
+            if (int rc = make_map(mb_, b_ptr[h], d.K, d.N, b_ld, bn, false)) return rc;
+        }
     }
     if (pair) {
         if (int rc = launch_pair(p)) return rc;
@@ -885,7 +986,10 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
     } else {
         const long long work = tiles * p.splits;
         const int grid = (int)(work < rt().sm_count ? work : rt().sm_count);
-        tf32_gemm_kernel<<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
+        if (x3)
+            tf32_gemm_kernel<true><<<grid, kThreads, X3_SMEM_BYTES, rt().stream>>>(p);
+        else
+            tf32_gemm_kernel<false><<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
         count_launch();
         if (int rc = check_cuda(cudaGetLastError(), "TF32 GEMM launch")) return rc;
         if (p.splits > 1) {

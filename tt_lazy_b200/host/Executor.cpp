@@ -832,9 +832,11 @@ int gemm_path() {
     int p = tt_lazy::get_gemm_path();
     if (p < 0) {
         const char* e = getenv("TT_LAZY_GEMM");
-        p = (e && std::string(e) == "ffma") ? (int)TTC_GEMM_FFMA
-            : (e && std::string(e) == "tf32") ? (int)TTC_GEMM_TF32
-                                              : (int)TTC_GEMM_AUTO;
+        const std::string v = e ? e : "";
+        p = v == "ffma" ? (int)TTC_GEMM_FFMA
+            : v == "tf32" ? (int)TTC_GEMM_TF32
+            : v == "tf32x3" ? (int)TTC_GEMM_TF32X3
+                            : (int)TTC_GEMM_AUTO;
         tt_lazy::set_gemm_path(p);
     }
     return p;

@@ -202,9 +202,18 @@ PYBIND11_MODULE(_tt_lazy, m) {
         }
         return out;
     });
-    m.def("set_gemm_path", [](const std::string& p) {
-        tt_lazy::set_gemm_path(p == "ffma" ? TTC_GEMM_FFMA : p == "tf32" ? TTC_GEMM_TF32 : TTC_GEMM_AUTO);
-    });
+    m.def(
+        "set_gemm_path",
+        [](const std::string& p) {
+            if (p != "auto" && p != "ffma" && p != "tf32" && p != "tf32x3")
+                throw std::invalid_argument("gemm path must be auto, ffma, tf32 or tf32x3");
+            tt_lazy::set_gemm_path(p == "ffma"     ? TTC_GEMM_FFMA
+                                   : p == "tf32"   ? TTC_GEMM_TF32
+                                   : p == "tf32x3" ? TTC_GEMM_TF32X3
+                                                   : TTC_GEMM_AUTO);
+        },
+        "matmul path: auto (TF32 where the tensor-core kernel takes the shape), ffma, tf32, or tf32x3 "
+        "(fp32-accurate 3-pass TF32)");
     m.def("synchronize", []() {
         if (tt_lazy::backend_ready() && ttc_synchronize() != TTC_OK) throw std::runtime_error(ttc_last_error());
     });
