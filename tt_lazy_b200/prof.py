@@ -1,6 +1,6 @@
 """Small, self-contained launches of the hot kernels for profiling.
 
-    python -m tt_lazy_b200.prof gemm [M]      # tf32_gemm_kernel: X[M,4096] . W[4096,16384], 3 launches
+    python -m tt_lazy_b200.prof gemm [M] [tf32|tf32x3]  # tf32_gemm_kernel: X[M,4096] . W[4096,16384], 3 launches
     python -m tt_lazy_b200.prof chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
     python -m tt_lazy_b200.prof small_mlp      # the small MLP workload through tl.Plan, 3 runs
 
@@ -26,16 +26,17 @@ def _setup():
     return torch, ttc
 
 
-def gemm(M=8192, N=16384, K=4096, reps=3):
+def gemm(M=8192, N=16384, K=4096, reps=3, path="tf32"):
     torch, ttc = _setup()
     g = torch.Generator(device="cuda").manual_seed(2)
     a = torch.randn(M, K, device="cuda", generator=g)
     b = torch.randn(K, N, device="cuda", generator=g) / 64
     c = torch.empty(M, N, device="cuda")
     for _ in range(reps):
-        ttc.gemm(M, N, K, a.data_ptr(), K, b.data_ptr(), N, c.data_ptr(), N, path=ttc.GEMM_TF32)
+        ttc.gemm(M, N, K, a.data_ptr(), K, b.data_ptr(), N, c.data_ptr(), N,
+                 path=ttc.GEMM_TF32X3 if path == "tf32x3" else ttc.GEMM_TF32)
     torch.cuda.synchronize()
-    print(f"gemm {M}x{N}x{K} ok, c[0,0] = {float(c[0, 0]):.6g}")
+    print(f"gemm {path} {M}x{N}x{K} ok, c[0,0] = {float(c[0, 0]):.6g}")
 
 
 def chain(name="segments", N=8192, reps=3):
@@ -89,7 +90,7 @@ def main(argv):
         print(__doc__)
         return 2
     if argv[1] == "gemm":
-        gemm(int(argv[2]) if len(argv) > 2 else 8192)
+        gemm(int(argv[2]) if len(argv) > 2 else 8192, path=argv[3] if len(argv) > 3 else "tf32")
     else:
         chain(argv[2] if len(argv) > 2 else "segments", int(argv[3]) if len(argv) > 3 else 8192)
     return 0
