@@ -23,6 +23,14 @@ def normwise(got, want):
     return np.linalg.norm(got.astype(np.float64) - w) / max(np.linalg.norm(w), 1e-300)
 
 
+def ulp_dist(a, b):
+    a = np.ascontiguousarray(a, np.float32).view(np.int32).astype(np.int64)
+    b = np.ascontiguousarray(b, np.float32).view(np.int32).astype(np.int64)
+    a = np.where(a < 0, -(a & 0x7FFFFFFF), a)
+    b = np.where(b < 0, -(b & 0x7FFFFFFF), b)
+    return np.abs(a - b)
+
+
 def test_reference_known_answers():
     # test_end_to_end.cpp:58-89
     r = tl.matmul(tl.constant(np.full((2, 2), 2, np.float32)), tl.constant(np.full((2, 2), 3, np.float32)))
@@ -474,3 +482,68 @@ def test_guard_bands_find_no_overrun_and_catch_a_planted_one():
     finally:
         tl.set_canaries(False)
         tl.set_gemm_path("auto")
+
+
+SPECIALS = np.array([0.0, -0.0, 1e-45, -1e-45, 1.1754944e-38, -1.1754944e-38, 1.0, -1.0, 3.4028235e38,
+                     -3.4028235e38, np.inf, -np.inf, np.nan, 88.7, -88.7, 104.0, -104.0, 1e30, -1e30, 0.5],
+                    np.float32)
+
+
+def _same_bits_or_both_nan(got, want):
+    both_nan = np.isnan(got) & np.isnan(want)
+    return np.all(both_nan | (got.view(np.int32) == want.view(np.int32)))
+
+
+@pytest.mark.parametrize("shape", [(16, 64), (1024, 1024)])
+def test_special_values_through_fused_chains(shape):
+    """Zeros of both signs, subnormals, the float limits, infinities and NaN
+    through relu / add / multiply (bit-exact, NaN where the reference gives
+    NaN) and sigmoid (the correctly rounded formula): the small shape runs on
+    the interpreting kernels, the large one on the program-specialised ones."""
+    rng = np.random.default_rng(21)
+    x = rng.uniform(-2, 2, shape).astype(np.float32)
+    y = rng.uniform(-2, 2, shape).astype(np.float32)
+    for i in range(0, x.size, 97):
+        x.flat[i] = SPECIALS[(i // 97) % SPECIALS.size]
+        y.flat[i] = SPECIALS[(i // 97 + 7) % SPECIALS.size]
+    X, Y = tl.constant(x), tl.constant(y)
+    r = tl.relu(X)
+    chain = tl.multiply(tl.add(r, Y), tl.add(r, Y))
+    tl.evaluate([chain])
+    assert _same_bits_or_both_nan(chain.numpy(), oracle.multiply(oracle.add(oracle.relu(x), y),
+                                                               oracle.add(oracle.relu(x), y)))
+    s = tl.sigmoid(X)
+    got = s.numpy()
+    want = oracle.sigmoid_cr(x)
+    fin = ~np.isnan(want)
+    assert np.all(np.isnan(got[~fin]))
+    assert ulp_dist(got[fin], want[fin]).max() <= 1
+    assert np.all(got[x == np.inf] == 1.0) and np.all(got[x == -np.inf] == 0.0)
+    seg = tl.multiply(tl.sigmoid(X), tl.relu(tl.add(X, X)))
+    want = oracle.multiply(oracle.sigmoid_cr(x), oracle.relu(oracle.add(x, x)))
+    got = seg.numpy()
+    assert np.all(np.isnan(got) == np.isnan(want))
+    fin = ~np.isnan(want)
+    assert ulp_dist(got[fin], want[fin]).max() <= 1
+
+
+@pytest.mark.parametrize("path", ["ffma", "tf32"])
+def test_gemm_propagates_infinities_and_nan(path):
+    """A row of A holding +inf, another holding NaN: the product's rows are
+    +-inf / NaN exactly where the reference's fp32 matmul has them (inf * 0
+    gives NaN), the other rows stay finite and within the path's bound."""
+    tl.set_gemm_path(path)
+    rng = np.random.default_rng(22)
+    a = rng.standard_normal((256, 128)).astype(np.float32)
+    b = (rng.standard_normal((128, 256)) / 12).astype(np.float32)
+    b[5, :7] = 0.0
+    a[3, 5] = np.inf
+    a[9, 17] = np.nan
+    got = tl.matmul(tl.constant(a), tl.constant(b)).numpy()
+    want = oracle.matmul(a, b)
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    assert np.array_equal(np.isposinf(got), np.isposinf(want)) and np.array_equal(np.isneginf(got), np.isneginf(want))
+    fin = np.isfinite(want)
+    tol = 1e-5 if path == "ffma" else 2e-3
+    assert normwise(got[fin], want[fin]) <= tol
+    tl.set_gemm_path("auto")
