@@ -335,6 +335,10 @@ def run_ours(args):
     torch.cuda.set_device(local)
     import tt_lazy_b200 as tl
     from tt_lazy_b200 import capi
+    from tt_lazy_b200 import shard as _shard
+
+    # host staging buffers on the GPU's own socket (allocated after this)
+    numa_cpus = _shard.bind_host_to_gpu(local) if world > 1 else None
 
     tl.backend_init()
     dist = None
@@ -541,6 +545,7 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (X shard >= 128 MiB, W1/W2 256 MiB)"},
             "e2e": {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": ms_e2e,
                     "h2d_bytes_per_step": int(X.nbytes), "d2h_bytes_per_step": int(K1 * 4),
+                    "host_binding": (f"{len(numa_cpus)} CPUs of the GPU's NUMA node" if numa_cpus else "none"),
                     "path": f"tt_lazy Plan(pipeline_chunks={chunks}).run() over a streamed pinned-host X "
                             "(row chunks uploaded on a copy stream under the previous chunk's GEMMs) "
                             "+ to-host read of s"},

@@ -171,3 +171,20 @@ def test_collective_with_a_dead_peer_errors_within_the_timeout():
     kind, waited, _ = res[0]
     assert kind == "error"
     assert waited < 30.0
+
+
+def test_cpulist_parsing_and_gpu_numa_lookup(tmp_path):
+    """bind_host_to_gpu's topology lookup: the sysfs local_cpulist of the
+    GPU's PCI function (a fake sysfs tree here)."""
+    from tt_lazy_b200 import shard
+
+    assert shard.parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
+    assert shard.parse_cpulist("") == []
+    d = tmp_path / "0000:1b:00.0"
+    d.mkdir()
+    (d / "local_cpulist").write_text("56-111,168-223\n")
+    cpus = shard.gpu_local_cpus((0, 0x1B, 0), str(tmp_path))
+    assert cpus[0] == 56 and cpus[-1] == 223 and len(cpus) == 112
+    assert shard.gpu_local_cpus((0, 0x1C, 0), str(tmp_path)) is None
+    (d / "local_cpulist").write_text("garbage")
+    assert shard.gpu_local_cpus((0, 0x1B, 0), str(tmp_path)) is None

@@ -9,6 +9,10 @@
 * ``init_comm(world, rank, timeout_ms)`` -- creates the backend's NCCL
   communicator: rank 0's unique id travels over the already initialised
   ``torch.distributed`` process group (any backend, gloo included).
+* ``bind_host_to_gpu(device)`` -- pins the process to the CPUs of the GPU's
+  NUMA node (sysfs ``local_cpulist`` of its PCI function), so pinned host
+  buffers allocated afterwards are local to the GPU's socket and eight ranks'
+  host -> GPU copies do not cross the socket interconnect.
 * ``Heartbeat`` -- host-side failure detection between steps: every rank
   checks in on the process group's store before it launches a step's
   collective and raises ``PeerLost`` when a peer has not checked in within
@@ -17,6 +21,7 @@
 """
 from __future__ import annotations
 
+import os
 import time
 
 
@@ -46,6 +51,49 @@ def init_comm(world: int, rank: int, timeout_ms: int = 60000) -> None:
     obj = [uid]
     dist.broadcast_object_list(obj, src=0)
     tl.comm_init(world, rank, obj[0], timeout_ms)
+
+
+def parse_cpulist(text: str) -> list[int]:
+    """'0-3,8,10-11' -> [0, 1, 2, 3, 8, 10, 11] (the sysfs / cpuset list format)."""
+    cpus: list[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.extend(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def gpu_local_cpus(pci: tuple[int, int, int], sysfs: str = "/sys/bus/pci/devices") -> list[int] | None:
+    """CPUs local to the GPU at PCI (domain, bus, device), or None when sysfs
+    does not say (no such file, or an empty list)."""
+    domain, bus, dev = pci
+    path = os.path.join(sysfs, f"{domain:04x}:{bus:02x}:{dev:02x}.0", "local_cpulist")
+    try:
+        with open(path) as f:
+            cpus = parse_cpulist(f.read())
+    except (OSError, ValueError):
+        return None
+    return cpus or None
+
+
+def bind_host_to_gpu(device: int, sysfs: str = "/sys/bus/pci/devices") -> list[int] | None:
+    """Restricts this process to the CPUs of CUDA device `device`'s NUMA node
+    (intersected with the CPUs it may already use). Returns the CPUs bound
+    to, or None when nothing changed (no topology information, or no
+    overlap). Call before allocating pinned host buffers."""
+    import torch
+
+    p = torch.cuda.get_device_properties(device)
+    cpus = gpu_local_cpus((p.pci_domain_id, p.pci_bus_id, p.pci_device_id), sysfs)
+    if not cpus:
+        return None
+    allowed = os.sched_getaffinity(0)
+    use = [c for c in cpus if c in allowed]
+    if not use or set(use) == allowed:
+        return None
+    os.sched_setaffinity(0, use)
+    return use
 
 
 class PeerLost(RuntimeError):
