@@ -449,23 +449,36 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const __grid_const
     bool vv[4];
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-        const float4 t = __ldcg(reinterpret_cast<const float4*>(src + 4 * g));
-        v[g][0] = t.x;
-        v[g][1] = t.y;
-        v[g][2] = t.z;
-        v[g][3] = t.w;
         rr[g] = row;
         cc[g] = col0 + 4 * g;
         vv[g] = row < p.M && cc[g] < p.N;
     }
-    for (int sp = 1; sp < p.splits; ++sp) {
+    // Four splits' loads in flight per round trip; the adds stay in split order.
+    for (int s0 = 0; s0 < p.splits; s0 += 4) {
+        float4 t[4][4];
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-            const float4 t = __ldcg(reinterpret_cast<const float4*>(src + sp * p.split_stride + 4 * g));
-            v[g][0] += t.x;
-            v[g][1] += t.y;
-            v[g][2] += t.z;
-            v[g][3] += t.w;
+        for (int u = 0; u < 4; ++u)
+            if (s0 + u < p.splits)
+#pragma unroll
+                for (int g = 0; g < 4; ++g)
+                    t[u][g] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + u) * p.split_stride + 4 * g));
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            if (s0 + u >= p.splits) break;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                if (s0 + u == 0) {
+                    v[g][0] = t[u][g].x;
+                    v[g][1] = t[u][g].y;
+                    v[g][2] = t[u][g].z;
+                    v[g][3] = t[u][g].w;
+                } else {
+                    v[g][0] += t[u][g].x;
+                    v[g][1] += t[u][g].y;
+                    v[g][2] += t[u][g].z;
+                    v[g][3] += t[u][g].w;
+                }
+            }
         }
     }
     run_program<4, 4>(p.epi, v, 0, rr, cc, vv);
