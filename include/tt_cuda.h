@@ -204,10 +204,13 @@ typedef struct {
 int ttc_eltwise_chain(const ttc_chain_desc* desc);
 
 /* Same computation as ttc_eltwise_chain, for callers that must not allocate
- * device memory while they run: code inside a CUDA-graph capture, a serving
- * or real-time loop that forbids allocation after start-up, or a host
- * framework that owns every allocation itself. No counterpart in the
- * reference (its backend runs on the CPU and allocates a Tensor per op).
+ * device memory while they run: a serving or real-time loop that reserves
+ * all its memory at start-up (a cudaMalloc mid-request can stall on a device
+ * synchronisation or fail under memory pressure), or a host framework that
+ * owns every device allocation through its own pool, where a library
+ * allocating behind its back breaks the pool's accounting and limits. No
+ * counterpart in the reference (its backend runs on the CPU and allocates a
+ * Tensor per op).
  *
  * It calls no cudaMalloc, cudaFree or allocating library routine: the
  * per-block partial sums of a reduction go to a fixed 1 MiB device array

@@ -1,8 +1,9 @@
 """ttc_eltwise_chain_noalloc: the element-wise chain entry point for callers
-that cannot allocate device memory while they run (inside a CUDA-graph
-capture, in a serving loop that forbids allocation after start-up, or under
-a host framework that owns all memory). Its reduction scratch is a fixed
-1 MiB device array inside the library instead of library-allocated memory.
+that cannot allocate device memory while they run -- a serving loop that
+reserves all its memory at start-up (an allocation mid-request can stall or
+fail), or a host framework whose own pool owns every device allocation. Its
+reduction scratch is a fixed 1 MiB device array inside the library instead
+of library-allocated memory.
 
 Checked through the C-ABI against ttc_eltwise_chain on the same inputs, on
 two calls in a row (the shared scratch keeps the previous call's contents),

@@ -529,14 +529,15 @@ int ttc_reduce(const float* in, const uint32_t* shape, int rank, const int32_t* 
 
 // ----------------------------------------------------------------------------
 // Allocation-free variant of ttc_eltwise_chain, for callers that cannot
-// allocate device memory while they run: code inside a CUDA-graph capture,
-// a real-time or serving loop that forbids allocation after start-up, or a
-// host framework that owns every allocation itself. The only scratch the
+// allocate device memory while they run: a serving or real-time loop that
+// reserves all its memory at start-up (an allocation mid-request can stall on
+// a device synchronisation or fail under memory pressure), or a host
+// framework whose own pool owns every device allocation. The only scratch the
 // chain kernels need -- per-block partial sums of a reduction -- lives in a
 // file-scope device array of fixed size instead of the library workspace.
 namespace {
 constexpr size_t kNoAllocScratchFloats = 262144;  // 1 MiB; every GPU that loads the library holds it
-__device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 constexpr int kMaxDevices = 64;
 float* g_noalloc_scratch_dev[kMaxDevices] = {};  // device address of the array, per device
 }  // namespace
