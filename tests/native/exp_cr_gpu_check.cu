@@ -3,9 +3,12 @@
 //  2. exp_cr(x) against CUDA's double exp rounded to float, every float with
 //     |x| <= 104 (they differ only where the exact value is within ~2^-44 of
 //     a rounding midpoint);
-//  3. sigmoid_cr_n (one range test per vector) == sigmoid_cr per element on
-//     a sweep that includes NaN, +-inf and the slow-path range.
-// Prints "rcp_mismatch=<n> exp_mismatch=<n> exp_over1ulp=<n> vec_mismatch=<n>".
+//  3. sigmoid_cr_n (one range test per vector, packed pairs) == sigmoid_cr per
+//     element on a sweep that includes NaN, +-inf and the slow-path range;
+//  4. the packed pair reciprocal rcp_1p_x2(e) == __frcp_rn(1 + e) for every
+//     float e in [0, 2^126).
+// Prints "rcp_mismatch=<n> exp_mismatch=<n> exp_over1ulp=<n> vec_mismatch=<n>
+// rcp2_mismatch=<n>".
 // Every loop index stays below its bound; the kernels take no input buffers.
 #include <cstdio>
 #include <cuda_runtime.h>
@@ -49,22 +52,37 @@ __global__ void check(unsigned long long* out, unsigned top) {
     atomicAdd(&out[3], vec_bad);
 }
 
+__global__ void check_rcp2(unsigned long long* out) {
+    unsigned long long bad = 0;
+    const unsigned total = 0x7E800000u;  // bit patterns of [0, 2^126)
+    for (unsigned u = 2 * (blockIdx.x * blockDim.x + threadIdx.x); u + 1 < total; u += 2 * gridDim.x * blockDim.x) {
+        const float e0 = __int_as_float((int)u), e1 = __int_as_float((int)(u + 1));
+        float y0, y1;
+        rcp_1p_x2(e0, e1, y0, y1);
+        bad += __float_as_int(y0) != __float_as_int(__frcp_rn(__fadd_rn(1.0f, e0)));
+        bad += __float_as_int(y1) != __float_as_int(__frcp_rn(__fadd_rn(1.0f, e1)));
+    }
+    atomicAdd(&out[4], bad);
+}
+
 int main() {
     unsigned long long* d = nullptr;
-    if (cudaMalloc(&d, 4 * sizeof(unsigned long long)) != cudaSuccess) return 2;
-    cudaMemset(d, 0, 4 * sizeof(unsigned long long));
+    if (cudaMalloc(&d, 5 * sizeof(unsigned long long)) != cudaSuccess) return 2;
+    cudaMemset(d, 0, 5 * sizeof(unsigned long long));
     const float f104 = 104.0f;
     unsigned top;
     memcpy(&top, &f104, 4);
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
     check<<<sms * 8, 256>>>(d, top);
-    unsigned long long h[4] = {0, 0, 0, 0};
+    check_rcp2<<<sms * 8, 256>>>(d);
+    unsigned long long h[5] = {0, 0, 0, 0, 0};
     const cudaError_t e = cudaMemcpy(h, d, sizeof h, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) {
         printf("cuda error %s\n", cudaGetErrorString(e));
         return 1;
     }
-    printf("rcp_mismatch=%llu exp_mismatch=%llu exp_over1ulp=%llu vec_mismatch=%llu\n", h[0], h[1], h[2], h[3]);
+    printf("rcp_mismatch=%llu exp_mismatch=%llu exp_over1ulp=%llu vec_mismatch=%llu rcp2_mismatch=%llu\n", h[0], h[1],
+           h[2], h[3], h[4]);
     return 0;
 }

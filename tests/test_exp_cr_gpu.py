@@ -3,7 +3,9 @@
 the Markstein reciprocal equals the IEEE reciprocal (__frcp_rn) on every
 float in [1, 2^126); exp_cr differs from CUDA's double exp rounded to float
 only by single ulps at rounding midpoints; the vector sigmoid (one range test
-for several values) equals the scalar one, NaN and infinities included."""
+for several values, packed pairs) equals the scalar one, NaN and infinities
+included; the packed pair reciprocal equals __frcp_rn(1 + e) on every e in
+[0, 2^126)."""
 import os
 import re
 import shutil
@@ -25,10 +27,12 @@ def test_exp_and_reciprocal_on_device(tmp_path):
     subprocess.check_call([NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-fmad=false", "-std=c++17",
                            "-I" + CSRC, os.path.join(HERE, "native", "exp_cr_gpu_check.cu"), "-o", exe])
     out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=300).stdout
-    m = re.search(r"rcp_mismatch=(\d+) exp_mismatch=(\d+) exp_over1ulp=(\d+) vec_mismatch=(\d+)", out)
+    m = re.search(r"rcp_mismatch=(\d+) exp_mismatch=(\d+) exp_over1ulp=(\d+) vec_mismatch=(\d+) "
+                  r"rcp2_mismatch=(\d+)", out)
     assert m, out
-    rcp, exp_bad, exp_far, vec = map(int, m.groups())
+    rcp, exp_bad, exp_far, vec, rcp2 = map(int, m.groups())
     assert rcp == 0
     assert exp_far == 0
     assert exp_bad <= 32, exp_bad
     assert vec == 0
+    assert rcp2 == 0

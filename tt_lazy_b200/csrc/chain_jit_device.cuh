@@ -298,7 +298,11 @@ __device__ __forceinline__ void ttj_cols(const JParams& p) {
         for (int g = 0; g < G; ++g)
             if (valid[g])
 #pragma unroll
-                for (int w = 0; w < W; ++w) s[w] += acc[g][w];
+                for (int w = 0; w + 1 < W; w += 2) f32x2_add(s[w], s[w + 1], acc[g][w], acc[g][w + 1]);
+        if (W & 1)
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+                if (valid[g]) s[W - 1] += acc[g][W - 1];
 #pragma unroll
         for (int g = 0; g < G; ++g) {
             row[g] = nrow[g];

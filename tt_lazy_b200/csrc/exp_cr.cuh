@@ -374,14 +374,71 @@ __device__ __forceinline__ float sigmoid_cr(float x, const ExpCrTable& t) {
 
 // N values at once: one range test for all of them (the slow path is for
 // |x| > 87 only, which ordinary data never reaches).
+#if defined(__CUDACC__) || defined(__CUDACC_RTC__)
+// Packed fp32 pairs (sm_100 f32x2 instructions: two IEEE round-to-nearest
+// operations per instruction, the same results as two scalar ones).
+__device__ __forceinline__ void f32x2_add(float& a0, float& a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%0, %1};\n\tmov.b64 pb, {%2, %3};\n\t"
+        "add.rn.f32x2 pa, pa, pb;\n\tmov.b64 {%0, %1}, pa;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void f32x2_sub(float& a0, float& a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%0, %1};\n\tmov.b64 pb, {%2, %3};\n\t"
+        "sub.rn.f32x2 pa, pa, pb;\n\tmov.b64 {%0, %1}, pa;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void f32x2_mul(float& a0, float& a1, float b0, float b1) {
+    asm("{\n\t.reg .b64 pa, pb;\n\tmov.b64 pa, {%0, %1};\n\tmov.b64 pb, {%2, %3};\n\t"
+        "mul.rn.f32x2 pa, pa, pb;\n\tmov.b64 {%0, %1}, pa;\n\t}"
+        : "+f"(a0), "+f"(a1)
+        : "f"(b0), "f"(b1));
+}
+__device__ __forceinline__ void f32x2_fma(float& d0, float& d1, float a0, float a1, float b0, float b1, float c0,
+                                          float c1) {
+    asm("{\n\t.reg .b64 pa, pb, pc;\n\tmov.b64 pa, {%2, %3};\n\tmov.b64 pb, {%4, %5};\n\t"
+        "mov.b64 pc, {%6, %7};\n\tfma.rn.f32x2 pa, pa, pb, pc;\n\tmov.b64 {%0, %1}, pa;\n\t}"
+        : "=f"(d0), "=f"(d1)
+        : "f"(a0), "f"(a1), "f"(b0), "f"(b1), "f"(c0), "f"(c1));
+}
+
+// 1 / (1 + e) for two e >= 0 with 1 + e < 2^126, each equal to
+// rcp_rn_ge1(1 + e): the add and Markstein's correction as packed pairs.
+// d = 1 + e and -d = -1 - e are roundings of the same exact sum, so
+// y0 + y0 (1 - d y0) comes out bit-identical to the scalar form (checked on
+// every float e in [0, 2^126) on the device).
+__device__ __forceinline__ void rcp_1p_x2(float e0, float e1, float& y0, float& y1) {
+    float d0 = 1.0f, d1 = 1.0f, n0 = -1.0f, n1 = -1.0f;
+    f32x2_add(d0, d1, e0, e1);
+    f32x2_sub(n0, n1, e0, e1);
+    float a0, a1;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(a0) : "f"(d0));
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(a1) : "f"(d1));
+    float r0, r1;
+    f32x2_fma(r0, r1, n0, n1, a0, a1, 1.0f, 1.0f);
+    f32x2_fma(y0, y1, a0, a1, r0, r1, a0, a1);
+}
+
+__device__ __forceinline__ void sigmoid_cr_fast2(float& x0, float& x1, const ExpCrTable& t) {
+    rcp_1p_x2(exp_cr_fast(-x0, t), exp_cr_fast(-x1, t), x0, x1);
+}
+#endif
+
 template <int N>
 __device__ __forceinline__ void sigmoid_cr_n(float* v, const ExpCrTable& t) {
     bool fast = true;
 #pragma unroll
     for (int i = 0; i < N; ++i) fast = fast && fabsf(v[i]) <= 87.0f;  // false for NaN too
     if (fast) {
+#if defined(__CUDA_ARCH__) || defined(__CUDACC_RTC__)
+#pragma unroll
+        for (int i = 0; i + 1 < N; i += 2) sigmoid_cr_fast2(v[i], v[i + 1], t);
+        if (N & 1) v[N - 1] = sigmoid_cr_fast(v[N - 1], t);
+#else
 #pragma unroll
         for (int i = 0; i < N; ++i) v[i] = sigmoid_cr_fast(v[i], t);
+#endif
     } else {
 #pragma unroll
         for (int i = 0; i < N; ++i) v[i] = sigmoid_cr(v[i], t);
