@@ -352,6 +352,40 @@ def test_gemm_tf32_split_k(ttc, m, k, n, act, monkeypatch):
     assert normwise(got, whole) <= RTOL_TF32
 
 
+@pytest.mark.parametrize("path,m,n,k", [("tf32", 4096, 4096, 1024), ("tf32x3", 1664, 4864, 1024)])
+def test_gemm_tail_wave_split(ttc, path, m, n, k, monkeypatch):
+    """The opt-in split of a partly filled last wave (TTC_GEMM_TAILSPLIT=1;
+    4096x4096: 512 tiles = 3 waves of 148 + 68, only those 68 tiles split
+    along K): the same values as the unsplit launch up to fp32 summation
+    order, the fused column sums too, and sampled rows (the last row block
+    included) against the oracle."""
+    rng = np.random.default_rng(18)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    bias = rng.uniform(-0.1, 0.1, (1, n)).astype(np.float32)
+    A, B, Bv = dev(ttc, a), dev(ttc, b), dev(ttc, bias)
+    code = ttc.GEMM_TF32X3 if path == "tf32x3" else ttc.GEMM_TF32
+
+    def run():
+        C = ttc.DeviceArray.empty((m, n))
+        S = ttc.DeviceArray.empty((n,))
+        epi = ttc.chain_desc(m, n, [ttc.in_view(Bv.ptr, 0)], [ttc.out_view(C.ptr, n)],
+                             [ttc.instr(ttc.OP_ADD, ttc.SRC_INPUT, 0), ttc.instr(ttc.OP_SIGMOID),
+                              ttc.instr(ttc.OP_STORE, idx=0)], reduce=ttc.REDUCE_COLS, reduce_out=S.ptr)
+        ttc.gemm(m, n, k, A.ptr, k, B.ptr, n, path=code, epilogue=epi)
+        return C.numpy(), S.numpy()
+
+    monkeypatch.setenv("TTC_GEMM_TAILSPLIT", "1")
+    c1, s1 = run()
+    monkeypatch.setenv("TTC_GEMM_TAILSPLIT", "0")
+    c0, s0 = run()
+    assert normwise(c1, c0) <= 1e-6 and normwise(s1, s0) <= 1e-6
+    assert not np.array_equal(c1, c0) or path == "tf32x3"  # the split tiles sum in another order
+    rows = np.concatenate([rng.choice(m - 128, 48, replace=False), np.arange(m - 16, m)])
+    want = oracle.sigmoid_cr(oracle.add(oracle.matmul(a[rows], b), bias))
+    assert normwise(c1[rows], want) <= (RTOL_FFMA if path == "tf32x3" else RTOL_TF32)
+
+
 @pytest.mark.parametrize("m,k,n", [(256, 512, 1024), (384, 100, 300), (1000, 260, 772), (520, 64, 1032),
                                    (1024, 512, 1280)])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (1, 0), (0, 1), (1, 1)])

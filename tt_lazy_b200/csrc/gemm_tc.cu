@@ -60,14 +60,33 @@ struct TcParams {
     int* status;
     DProgram epi;
     float* partials;  // column sums of the final epilogue value per 32-row group, or null
-    // Split-K (single-CTA kernel only): work item w is split w % splits of
-    // tile w / splits, covering k-blocks [kb_per_split * split, ...). Each
-    // split stores its raw accumulator tile into split_ws, row-major
-    // [splits][m_blocks * BM][n_blocks * BN]; a second kernel adds the splits
-    // in split order and runs the epilogue on the sum.
-    int splits, kb_per_split;
+    // Split-K (single-CTA kernel only). Work items [0, full_tiles) are whole
+    // tiles 0 .. full_tiles - 1 with the fused epilogue; every later tile t
+    // is `splits` work items, split s covering k-blocks
+    // [kb_per_split * s, ...), each storing its raw accumulator tile into
+    // split_ws (tile-local, row-major BM x tile width, at slot
+    // (t - full_tiles) * splits + s); a second kernel adds a tile's splits in
+    // split order and runs the epilogue on the sum. full_tiles = 0 splits
+    // every tile (GEMMs with few tiles); full_tiles = the tiles of the full
+    // waves splits only the last, partly filled wave's tiles.
+    int full_tiles, splits, kb_per_split;
     float* split_ws;
 };
+
+__device__ __forceinline__ void work_item(const TcParams& p, int w, int& tile, int& split, int& kb0, int& kb1) {
+    if (w < p.full_tiles) {
+        tile = w;
+        split = -1;
+        kb0 = 0;
+        kb1 = p.k_blocks;
+        return;
+    }
+    const int v = w - p.full_tiles;
+    tile = p.full_tiles + v / p.splits;
+    split = v % p.splits;
+    kb0 = split * p.kb_per_split;
+    kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+}
 
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
@@ -197,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
-    const int num_work = p.m_blocks * p.n_blocks * p.splits;
+    const int num_work = p.full_tiles + (p.m_blocks * p.n_blocks - p.full_tiles) * p.splits;
     bool failed = false;
 
     if (warp == 0) {
@@ -208,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             uint32_t phase = 0;
             long long issued = 0;
             for (int w = blockIdx.x; w < num_work && !failed; w += gridDim.x) {
-                const int tile = w / p.splits, kb0 = (w % p.splits) * p.kb_per_split;
-                const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+                int tile, split, kb0, kb1;
+                work_item(p, w, tile, split, kb0, kb1);
                 int mb, nb;
                 tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
                 for (int kb = kb0; kb < kb1; ++kb) {
@@ -285,8 +304,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             uint32_t phase = 0;
             int t = 0;
             for (int w = blockIdx.x; w < num_work && !failed; w += gridDim.x, ++t) {
-                const int kb0 = (w % p.splits) * p.kb_per_split;
-                const int kb1 = min(p.k_blocks, kb0 + p.kb_per_split);
+                int tile, split, kb0, kb1;
+                work_item(p, w, tile, split, kb0, kb1);
                 const int b = t & 1;
                 const uint32_t acc_phase = (t >> 1) & 1;
                 if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
@@ -358,13 +377,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
         };
         int t = 0;
         for (int wi = blockIdx.x; wi < num_work; wi += gridDim.x, ++t) {
-            const int tile = wi / p.splits, split = wi % p.splits;
+            int tile, split, kb0, kb1;
+            work_item(p, wi, tile, split, kb0, kb1);
             int mb, nb;
             tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
             const int b = t & 1;
             const uint32_t acc_phase = (t >> 1) & 1;
             const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase));
-            if (p.splits == 1) {
+            if (split < 0) {
                 if (!ok) {
                     failed = true;
                     break;
@@ -391,9 +411,8 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                 break;
             }
             tc_fence_after();
-            const long long ld = (long long)p.n_blocks * TBN;
-            float* const dst = p.split_ws + ((long long)split * p.m_blocks * BM + (long long)mb * BM + q * 32 + lane) * ld +
-                               (long long)nb * TBN;
+            const long long slot = (long long)(tile - p.full_tiles) * p.splits + split;
+            float* const dst = p.split_ws + (slot * BM + q * 32 + lane) * TBN;
             for (int c = 0; c < TBN / 32; ++c) {
                 uint32_t r[32];
                 tc_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * TBN + c * 32), r);
@@ -419,16 +438,15 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                      : "memory");
 }
 
-// Split-K epilogue: one warp per (32-row group, 16-column group), lane = row.
-// Adds the splits in split order (deterministic), then runs the epilogue
-// program and, for a fused column sum, writes the same per-32-row-group
-// partials as the GEMM epilogue (every group of the padded row range, rows
-// past M contributing zeros).
+// Split-K epilogue: one warp per (split tile, 32-row group, 16-column group),
+// lane = row. Adds the tile's splits in split order (deterministic), then runs
+// the epilogue program and, for a fused column sum, writes the same
+// per-32-row-group partials as the GEMM epilogue (rows past M contributing
+// zeros).
 struct SplitEpiParams {
     const float* ws;
-    long long ld, split_stride;  // row stride of a split, elements between splits
-    int splits, M, N;
-    long long row_groups;        // padded rows / 32
+    int full_tiles, split_tiles, splits, tile_n;  // tile_n: tile width (256, 128 for TF32X3)
+    int m_blocks, n_blocks, M, N;
     DProgram epi;
     float* partials;
 };
@@ -437,13 +455,18 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const __grid_const
     if (p.epi.has_sigmoid) exp2_table_init_block();
     __syncthreads();
     const int lane = threadIdx.x & 31;
-    const int cgroups = (p.N + 15) / 16;
+    const int cg_per_tile = p.tile_n / 16, warps_per_tile = (BM / 32) * cg_per_tile;
     const long long warp_id = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-    if (warp_id >= p.row_groups * cgroups) return;  // whole warps only
-    const long long rg = warp_id / cgroups;
-    const long long col0 = (long long)(warp_id % cgroups) * 16;
-    const long long row = rg * 32 + lane;
-    const float* src = p.ws + row * p.ld + col0;
+    if (warp_id >= (long long)p.split_tiles * warps_per_tile) return;  // whole warps only
+    const int tt = (int)(warp_id / warps_per_tile), rem = (int)(warp_id % warps_per_tile);
+    const int q = rem / cg_per_tile, cg = rem % cg_per_tile;
+    int mb, nb;
+    tile_coords(p.full_tiles + tt, p.m_blocks, p.n_blocks, mb, nb);
+    const long long row = (long long)mb * BM + q * 32 + lane;
+    const long long col0 = (long long)nb * p.tile_n + cg * 16;
+    if (col0 >= p.N) return;  // warp-uniform
+    const long long split_stride = (long long)BM * p.tile_n;
+    const float* src = p.ws + ((long long)tt * p.splits * BM + q * 32 + lane) * p.tile_n + cg * 16;
     float v[4][4];
     long long rr[4], cc[4];
     bool vv[4];
@@ -461,7 +484,7 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const __grid_const
             if (s0 + u < p.splits)
 #pragma unroll
                 for (int g = 0; g < 4; ++g)
-                    t[u][g] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + u) * p.split_stride + 4 * g));
+                    t[u][g] = __ldcg(reinterpret_cast<const float4*>(src + (s0 + u) * split_stride + 4 * g));
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             if (s0 + u >= p.splits) break;
@@ -487,6 +510,7 @@ __global__ void __launch_bounds__(256) splitk_epilogue_kernel(const __grid_const
         for (int g = 0; g < 4; ++g)
 #pragma unroll
             for (int w = 0; w < 4; ++w) v[g][w] = vv[g] ? v[g][w] : 0.0f;
+        const long long rg = (long long)mb * (BM / 32) + q;
         warp_col_sums16(v, p.partials + rg * p.N + col0, lane, p.N - col0);
     }
 }
@@ -896,6 +920,36 @@ int split_count(long long tiles, int k_blocks, int sms) {
     return (int)std::max<long long>(1, std::min<long long>(std::min<long long>(fill, k_blocks / 2), 16));
 }
 
+// Split of the last, partly filled wave (opt-in: TTC_GEMM_TAILSPLIT=1, read
+// at every call). With W full waves of `sms` tiles and R < sms tiles left, a
+// wave model says the launch takes W + 1 wave times and splitting the R tiles
+// along K into s parts takes W + ceil(R s / sms) / s (4096x4096 on 148 SMs:
+// 3 + 68 tiles -> 3.5 instead of 4). Measured, the partly filled wave is much
+// shorter than a full one (its CTAs share the L2 bandwidth that bounds this
+// kernel with fewer others): 4096^3 gained 3 % (229 vs 236 us), 4096x4096x1024
+// lost 10 % and 2048x4096x16384 lost 1 % to the extra epilogue launch and the
+// partial tiles' traffic, so it is not the default. Returns s (1: no split)
+// and the number of whole tiles in *full.
+int tail_split(long long tiles, int k_blocks, int sms, int* full) {
+    const char* e = getenv("TTC_GEMM_TAILSPLIT");
+    if (!(e && e[0] == '1') || tiles < sms || k_blocks < 32) return 1;
+    const long long waves = tiles / sms, rest = tiles % sms;
+    if (rest == 0) return 1;
+    int best = 1;
+    double best_t = (double)(waves + 1);
+    for (int s = 2; s <= 4; ++s) {
+        if (k_blocks < 2 * s) break;
+        const double t = (double)waves + (double)((rest * s + sms - 1) / sms) / s;
+        if (t < best_t - 1e-9) {
+            best_t = t;
+            best = s;
+        }
+    }
+    if (best == 1 || best_t > 0.95 * (double)(waves + 1)) return 1;
+    *full = (int)(waves * sms);
+    return best;
+}
+
 }  // namespace
 
 void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg, float* out, long long sseg, int mean,
@@ -948,17 +1002,36 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
     const long long groups = (long long)p.m_blocks * (tm / 32);  // every 32-row group of every row tile
     if (reduce_out && groups > INT32_MAX)
         return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many rows for the fused column sum");
-    p.splits = pair ? 1 : split_count(tiles, p.k_blocks, rt().sm_count);
+    // split-K: every tile when there are few (or, opt-in, the tiles of a
+    // partly filled last wave)
+    p.full_tiles = (int)tiles;
+    p.splits = 1;
+    if (!pair) {
+        const int s = split_count(tiles, p.k_blocks, rt().sm_count);
+        if (s > 1) {
+            p.full_tiles = 0;
+            p.splits = s;
+        } else {
+            int full = 0;
+            const int ts = tail_split(tiles, p.k_blocks, rt().sm_count, &full);
+            if (ts > 1) {
+                p.full_tiles = full;
+                p.splits = ts;
+            }
+        }
+    }
     p.kb_per_split = (p.k_blocks + p.splits - 1) / p.splits;
     p.splits = (p.k_blocks + p.kb_per_split - 1) / p.kb_per_split;  // every split has k-blocks
+    if (p.splits == 1) p.full_tiles = (int)tiles;
+    const long long split_tiles = tiles - p.full_tiles;
     const size_t part_bytes = reduce_out ? ((size_t)groups * d.N * sizeof(float) + 255) & ~(size_t)255 : 0;
-    const long long mp = (long long)p.m_blocks * BM, np = (long long)p.n_blocks * tn;
-    const size_t split_bytes = p.splits > 1 ? ((size_t)p.splits * mp * np * sizeof(float) + 255) & ~(size_t)255 : 0;
+    const size_t split_bytes =
+        split_tiles ? ((size_t)split_tiles * p.splits * BM * tn * sizeof(float) + 255) & ~(size_t)255 : 0;
     if (part_bytes + split_bytes + x3_bytes) {
         void* ws = nullptr;
         if (int rc = workspace(part_bytes + split_bytes + x3_bytes, &ws)) return rc;
         if (reduce_out) p.partials = (float*)ws;
-        if (p.splits > 1) p.split_ws = (float*)((char*)ws + part_bytes);
+        if (split_tiles) p.split_ws = (float*)((char*)ws + part_bytes);
         if (x3) {
             char* x = (char*)ws + part_bytes + split_bytes;
             float* parts[4] = {(float*)x, (float*)(x + a_part), (float*)(x + 2 * a_part),
@@ -997,7 +1070,7 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
         if (int rc = launch_pair(p)) return rc;
         if (int rc = check_cuda(cudaGetLastError(), "TF32 pair GEMM launch")) return rc;
     } else {
-        const long long work = tiles * p.splits;
+        const long long work = p.full_tiles + split_tiles * p.splits;
         const int grid = (int)(work < rt().sm_count ? work : rt().sm_count);
         if (x3)
             tf32_gemm_kernel<true><<<grid, kThreads, X3_SMEM_BYTES, rt().stream>>>(p);
@@ -1005,19 +1078,21 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
             tf32_gemm_kernel<false><<<grid, kThreads, SMEM_BYTES, rt().stream>>>(p);
         count_launch();
         if (int rc = check_cuda(cudaGetLastError(), "TF32 GEMM launch")) return rc;
-        if (p.splits > 1) {
+        if (split_tiles) {
             SplitEpiParams e;
             std::memset(&e, 0, sizeof e);
             e.ws = p.split_ws;
-            e.ld = np;
-            e.split_stride = mp * np;
+            e.full_tiles = p.full_tiles;
+            e.split_tiles = (int)split_tiles;
             e.splits = p.splits;
+            e.tile_n = tn;
+            e.m_blocks = p.m_blocks;
+            e.n_blocks = p.n_blocks;
             e.M = d.M;
             e.N = d.N;
-            e.row_groups = mp / 32;
             e.epi = epi;
             e.partials = p.partials;
-            const long long warps = e.row_groups * ((d.N + 15) / 16);
+            const long long warps = split_tiles * (BM / 32) * (tn / 16);
             splitk_epilogue_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, rt().stream>>>(e);
             count_launch();
             if (int rc = check_cuda(cudaGetLastError(), "split-K epilogue launch")) return rc;
