@@ -284,11 +284,12 @@ int ttc_copy2d(const float* in, int64_t in_ld, float* out, int64_t out_ld, int64
  *                         (big*big + big*small + small*big) into fp32 TMEM
  *                         accumulators (the 1e-5 bound, ~1e-6 measured);
  *                         shapes the tensor-core kernel does not take run on
- *                         the FFMA path. Finite inputs only: an infinity
- *                         meets the other operand's remainder, which is
- *                         often exactly zero, so a product that fp32 gives
- *                         as +-inf can come out NaN (use FFMA or TF32 for
- *                         data with infinities).
+ *                         the FFMA path. An output tile whose rows of A or
+ *                         columns of B hold an infinity or NaN takes the
+ *                         big*big product alone (an infinity times a zero
+ *                         remainder would make NaN where fp32 gives +-inf):
+ *                         infinities and NaN come out where fp32 gives them,
+ *                         and that tile's finite values have TF32 accuracy.
  */
 typedef enum { TTC_GEMM_AUTO = 0, TTC_GEMM_FFMA = 1, TTC_GEMM_TF32 = 2, TTC_GEMM_TF32X3 = 3 } ttc_gemm_path;
 

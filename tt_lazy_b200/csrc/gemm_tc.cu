@@ -71,6 +71,10 @@ struct TcParams {
     // waves splits only the last, partly filled wave's tiles.
     int full_tiles, splits, kb_per_split;
     float* split_ws;
+    // TF32X3: nonzero where a row block of A / a column block of B holds an
+    // infinity or NaN; such tiles take the big * big product alone.
+    const int* nonfinite_a;
+    const int* nonfinite_b;
 };
 
 __device__ __forceinline__ void work_item(const TcParams& p, int w, int& tile, int& split, int& kb0, int& kb1) {
@@ -306,6 +310,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             for (int w = blockIdx.x; w < num_work && !failed; w += gridDim.x, ++t) {
                 int tile, split, kb0, kb1;
                 work_item(p, w, tile, split, kb0, kb1);
+                bool cross = X3;  // the big * small + small * big terms
+                if (X3 && p.nonfinite_a) {
+                    // An infinity times the other operand's remainder, which is
+                    // often exactly zero, would make NaN where fp32 gives +-inf.
+                    int mb, nb;
+                    tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
+                    cross = !(__ldcg(p.nonfinite_a + mb) | __ldcg(p.nonfinite_b + nb));
+                }
                 const int b = t & 1;
                 const uint32_t acc_phase = (t >> 1) & 1;
                 if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
@@ -326,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                         const uint64_t ad = make_desc(a_s + k * a_kstep, a_lbo, a_sbo, a_lay);
                         const uint64_t bd = make_desc(b_s + k * b_kstep, b_lbo, b_sbo, b_lay);
                         tc_mma_tf32(d_tmem, ad, bd, p.idesc, (kb != kb0 || k != 0) ? 1u : 0u);
-                        if (X3) {  // + big * small + small * big
+                        if (cross) {  // + big * small + small * big
                             const uint32_t a2_s = b_s + TB_BYTES, b2_s = a2_s + A_BYTES;
                             const uint64_t ad2 = make_desc(a2_s + k * a_kstep, a_lbo, a_sbo, a_lay);
                             const uint64_t bd2 = make_desc(b2_s + k * b_kstep, b_lbo, b_sbo, b_lay);
@@ -828,9 +840,12 @@ __device__ __forceinline__ float tf32_rn(float x) {
 // Rows of a stored operand (rows x cols, leading dimension lds) into dense
 // big / small copies with leading dimension ldd; blocks stride over rows,
 // threads over columns (coalesced).
+// A non-finite element sets flags[(by_col ? c : r) / blk]: the row block of
+// A or the column block of B (in output-tile units) it belongs to.
 __global__ void __launch_bounds__(256) tf32_split_kernel(const float* __restrict__ src, long long rows, long long cols,
                                                          long long lds, float* __restrict__ big,
-                                                         float* __restrict__ small, long long ldd) {
+                                                         float* __restrict__ small, long long ldd, int* flags,
+                                                         int by_col, int blk) {
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
         for (long long c = threadIdx.x; c < cols; c += blockDim.x) {
             const float x = __ldg(src + r * lds + c);
@@ -838,6 +853,7 @@ __global__ void __launch_bounds__(256) tf32_split_kernel(const float* __restrict
             const bool finite = (__float_as_uint(x) & 0x7f800000u) != 0x7f800000u;
             big[r * ldd + c] = b;
             small[r * ldd + c] = finite ? tf32_rn(__fsub_rn(x, b)) : 0.0f;
+            if (!finite) atomicOr(flags + (by_col ? c : r) / blk, 1);
         }
     }
 }
@@ -980,7 +996,7 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
     const long long a_ld = x3 ? (a_cols + 3) & ~3ll : d.lda, b_ld = x3 ? (b_cols + 3) & ~3ll : d.ldb;
     const size_t a_part = ((size_t)a_rows * a_ld * sizeof(float) + 255) & ~(size_t)255;
     const size_t b_part = ((size_t)b_rows * b_ld * sizeof(float) + 255) & ~(size_t)255;
-    const size_t x3_bytes = x3 ? 2 * (a_part + b_part) : 0;
+    size_t x3_bytes = x3 ? 2 * (a_part + b_part) : 0;  // + the non-finite block flags (below)
     const float* a_ptr[2] = {d.a, nullptr};
     const float* b_ptr[2] = {d.b, nullptr};
     p.M = d.M;
@@ -1027,6 +1043,7 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
     const size_t part_bytes = reduce_out ? ((size_t)groups * d.N * sizeof(float) + 255) & ~(size_t)255 : 0;
     const size_t split_bytes =
         split_tiles ? ((size_t)split_tiles * p.splits * BM * tn * sizeof(float) + 255) & ~(size_t)255 : 0;
+    if (x3) x3_bytes += ((size_t)(p.m_blocks + p.n_blocks) * sizeof(int) + 255) & ~(size_t)255;
     if (part_bytes + split_bytes + x3_bytes) {
         void* ws = nullptr;
         if (int rc = workspace(part_bytes + split_bytes + x3_bytes, &ws)) return rc;
@@ -1036,13 +1053,20 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
             char* x = (char*)ws + part_bytes + split_bytes;
             float* parts[4] = {(float*)x, (float*)(x + a_part), (float*)(x + 2 * a_part),
                                (float*)(x + 2 * a_part + b_part)};
+            int* flags = (int*)(x + 2 * (a_part + b_part));  // [m_blocks] for A, then [n_blocks] for B
+            TTC_CUDA(cudaMemsetAsync(flags, 0, (size_t)(p.m_blocks + p.n_blocks) * sizeof(int), rt().stream));
             const int sms = rt().sm_count;
+            // A stored [M, K]: its row r is output row r; stored [K, M]: column c is.
             tf32_split_kernel<<<(unsigned)std::min<long long>(a_rows, 8ll * sms), 256, 0, rt().stream>>>(
-                d.a, a_rows, a_cols, d.lda, parts[0], parts[1], a_ld);
+                d.a, a_rows, a_cols, d.lda, parts[0], parts[1], a_ld, flags, d.trans_a ? 1 : 0, BM);
             count_launch();
+            // B stored [K, N]: its column c is output column c; stored [N, K]: row r is.
             tf32_split_kernel<<<(unsigned)std::min<long long>(b_rows, 8ll * sms), 256, 0, rt().stream>>>(
-                d.b, b_rows, b_cols, d.ldb, parts[2], parts[3], b_ld);
+                d.b, b_rows, b_cols, d.ldb, parts[2], parts[3], b_ld, flags + p.m_blocks, d.trans_b ? 0 : 1,
+                tn);
             count_launch();
+            p.nonfinite_a = flags;
+            p.nonfinite_b = flags + p.m_blocks;
             if (int rc = check_cuda(cudaGetLastError(), "TF32X3 operand split launch")) return rc;
             a_ptr[0] = parts[0];
             a_ptr[1] = parts[1];
