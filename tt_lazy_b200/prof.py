@@ -1,6 +1,6 @@
 """Small, self-contained launches of the hot kernels for profiling.
 
-    python -m tt_lazy_b200.prof gemm [M] [tf32|tf32x3]  # tf32_gemm_kernel: X[M,4096] . W[4096,16384], 3 launches
+    python -m tt_lazy_b200.prof gemm [M] [tf32|tf32x3|ffma]  # the GEMM path's kernel: X[M,4096] . W[4096,16384], 3 launches
     python -m tt_lazy_b200.prof chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
     python -m tt_lazy_b200.prof small_mlp      # the small MLP workload through tl.Plan, 3 runs
 
@@ -34,7 +34,7 @@ def gemm(M=8192, N=16384, K=4096, reps=3, path="tf32"):
     c = torch.empty(M, N, device="cuda")
     for _ in range(reps):
         ttc.gemm(M, N, K, a.data_ptr(), K, b.data_ptr(), N, c.data_ptr(), N,
-                 path=ttc.GEMM_TF32X3 if path == "tf32x3" else ttc.GEMM_TF32)
+                 path={"tf32x3": ttc.GEMM_TF32X3, "ffma": ttc.GEMM_FFMA}.get(path, ttc.GEMM_TF32))
     torch.cuda.synchronize()
     print(f"gemm {path} {M}x{N}x{K} ok, c[0,0] = {float(c[0, 0]):.6g}")
 
