@@ -3,6 +3,7 @@
     python -m tt_lazy_b200.prof gemm [M] [tf32|tf32x3|ffma]  # the GEMM path's kernel: X[M,4096] . W[4096,16384], 3 launches
     python -m tt_lazy_b200.prof chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
     python -m tt_lazy_b200.prof small_mlp      # the small MLP workload through tl.Plan, 3 runs
+    python -m tt_lazy_b200.prof transpose [N]  # transpose_kernel on an N x N fp32 input, 3 launches
 
 NAME: copy | readme (relu -> add -> multiply, stored, summed) | sigmoid |
 segments (sigmoid(C) * relu(C + C) over 8 row segments, column sums).
@@ -67,6 +68,18 @@ def chain(name="segments", N=8192, reps=3):
     print(f"chain {name} {N}x{N} ok")
 
 
+def transpose(N=8192, reps=3):
+    torch, ttc = _setup()
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.rand(N, N, device="cuda", generator=g)
+    y = torch.empty_like(x)
+    for _ in range(reps):
+        ttc.transpose(x.data_ptr(), y.data_ptr(), 1, N, N)
+    torch.cuda.synchronize()
+    assert bool((y[:64, :64] == x[:64, :64].T).all())
+    print(f"transpose {N}x{N} ok")
+
+
 def small_mlp(reps=3):
     import torch
 
@@ -85,6 +98,9 @@ def small_mlp(reps=3):
 def main(argv):
     if len(argv) >= 2 and argv[1] == "small_mlp":
         small_mlp()
+        return 0
+    if len(argv) >= 2 and argv[1] == "transpose":
+        transpose(int(argv[2]) if len(argv) > 2 else 8192)
         return 0
     if len(argv) < 2 or argv[1] not in ("gemm", "chain"):
         print(__doc__)
