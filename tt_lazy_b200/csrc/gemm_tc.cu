@@ -926,14 +926,22 @@ int launch_pair(TcParams& p) {
 }
 
 // Split-K for GEMMs with too few output tiles to occupy the GPU (the small
-// MLP's 256 x 1024 x 512 is 8 tiles on 148 SMs): about one work item per SM,
-// at least 2 k-blocks (64 deep) per split, at most 16 splits. Off with
-// TTC_GEMM_SPLITK=0 (read at every call).
+// MLP's 256 x 1024 x 512 is 8 tiles on 148 SMs): at most one work item per
+// SM, at least 4 k-blocks (128 deep) per split, at most 16 splits. Fewer,
+// deeper splits write and re-read fewer partial tiles: the small MLP ran at
+// 34.9 us per graph replay with 4 k-blocks per split, 41.0 with 2 (3 and 8
+// measured as 4). Off with TTC_GEMM_SPLITK=0; TTC_GEMM_SPLITK_MAX and
+// TTC_GEMM_SPLITK_MINKB override the cap and the depth (read at every call,
+// for tuning sweeps).
 int split_count(long long tiles, int k_blocks, int sms) {
     const char* e = getenv("TTC_GEMM_SPLITK");
-    if ((e && e[0] == '0') || tiles * 2 > sms || k_blocks < 4) return 1;
+    if ((e && e[0] == '0') || tiles * 2 > sms || k_blocks < 8) return 1;
     const long long fill = (sms + tiles - 1) / tiles;
-    return (int)std::max<long long>(1, std::min<long long>(std::min<long long>(fill, k_blocks / 2), 16));
+    const char* m = getenv("TTC_GEMM_SPLITK_MAX");  // tuning sweeps
+    const long long cap = m && atoi(m) >= 2 ? atoi(m) : 16;
+    const char* q = getenv("TTC_GEMM_SPLITK_MINKB");
+    const long long min_kb = q && atoi(q) >= 1 ? atoi(q) : 4;
+    return (int)std::max<long long>(1, std::min<long long>(std::min<long long>(fill, k_blocks / min_kb), cap));
 }
 
 // Split of the last, partly filled wave (opt-in: TTC_GEMM_TAILSPLIT=1, read
