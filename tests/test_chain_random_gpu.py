@@ -4,9 +4,11 @@ Seeded random chain programs -- LOAD, RELU, SIGMOID, ADD / MUL with the
 accumulator, an input or a saved slot, SAVE, STORE -- over random operand
 views (full, row-broadcast [1, C] as in the reference's bias add, column-
 broadcast [R, 1]), segment counts and reductions (none, all, rows, columns,
-sum or mean), on shapes that reach every kernel family: the register
-interpreters (small or ragged: cols not a multiple of 4), the TMA-staged
-interpreter and the program-specialised NVRTC kernels (>= 1 Mi elements).
+sum or mean), on shapes that reach the register interpreters (small or
+ragged: cols not a multiple of 4) and the program-specialised NVRTC kernels
+(from 256 Ki elements); the same programs run once more in a fresh process
+with the specialised kernels off, where the large layouts take the
+TMA-staged interpreter.
 
 Bounds, as in the other parity tests: stored results are bit-exact against
 the oracle's IEEE float32 steps when the program has no sigmoid (sigmoid is
@@ -14,6 +16,10 @@ within 1 ulp of the correctly rounded formula, so programs with one get a
 few ulps after later steps); reductions are within 1e-5 of the fp64 sum of
 the oracle's own element values, relative to the sum of magnitudes.
 """
+import os
+import subprocess
+import sys
+
 import numpy as np
 import pytest
 
@@ -150,3 +156,13 @@ def test_random_chain_matches_oracle(ttc, seed):
         assert (np.abs(got[fin] - want[fin]) <= 1e-5 * scale[fin]).all(), (prog, reduce)
         nan = np.isnan(want)
         assert np.isnan(got[nan]).all(), (prog, reduce)
+
+
+def test_random_chains_on_the_staged_interpreter():
+    """The programs above with the specialised kernels switched off
+    (TTC_CHAIN_JIT=0, read once per process, so in a fresh one): the layouts
+    of 1 Mi elements and more run on the TMA-staged interpreter."""
+    env = dict(os.environ, TTC_CHAIN_JIT="0")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-x", "-p", "no:cacheprovider", "-k",
+                        "test_random_chain_matches_oracle"], env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

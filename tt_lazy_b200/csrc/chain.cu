@@ -388,7 +388,11 @@ static int run_chain_impl(const ttc_chain_desc& d, const FixedScratch* fixed) {
         if (int rc = launch_chain_jit(d, p.prog, &launched)) return rc;
         if (launched) return TTC_OK;
     }
-    if (tma_enabled && !fixed) {
+    // The TMA-staged interpreter pays for its pipeline set-up only on large
+    // problems (on 1000 x 1000 it replayed the README chain in 10.2 us, the
+    // register interpreter in 8.2): it serves layouts the specialised kernel
+    // declines, from 1 Mi elements.
+    if (tma_enabled && !fixed && (long long)d.rows * d.cols * d.nseg >= (1LL << 20)) {
         bool launched = false;
         if (int rc = launch_chain_tma(d, p.prog, &launched)) return rc;
         if (launched) return TTC_OK;
