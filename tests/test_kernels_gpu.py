@@ -358,7 +358,9 @@ def test_gemm_tail_wave_split(ttc, path, m, n, k, monkeypatch):
     4096x4096: 512 tiles = 3 waves of 148 + 68, only those 68 tiles split
     along K): the same values as the unsplit launch up to fp32 summation
     order, the fused column sums too, and sampled rows (the last row block
-    included) against the oracle."""
+    included) against the oracle. The single-CTA kernel is forced: the CTA-pair
+    kernel, the default for this many tiles, does not split."""
+    monkeypatch.setenv("TTC_GEMM_PAIR", "0")
     rng = np.random.default_rng(18)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)

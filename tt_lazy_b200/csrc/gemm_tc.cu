@@ -881,15 +881,23 @@ bool tf32_supported(const ttc_gemm_desc& d, const DProgram& epi, bool epi_vec) {
 
 namespace {
 
-// The CTA-pair kernel runs when TTC_GEMM_PAIR=1 (read at every call) and the
-// GEMM has at least one 256x256 tile. It is not the default: alone (burst
-// clocks) it is up to ~10% faster than the single-CTA kernel, but inside the
-// long power-capped MLP step both are held to the 1 kW limit and the pair
-// kernel's SM clock drops further (measured back to back: 496-499 vs 507-517
-// TFLOP/s per step, 1.07-1.09 vs 1.28-1.31 GHz), so the step is ~3% slower.
-bool use_pair(const ttc_gemm_desc& d) {
+// The CTA-pair kernel (cta_group::2, 256x256 per pair) runs by default when
+// its tiles fill the GPU: at least one tile per CTA pair (sms / 2). Measured
+// back to back on the large MLP step (power-capped at 1 kW, both kernels held
+// to the same clocks), the device-resident step rate is the same (553 / 550
+// vs 552 / 550 TFLOP/s) and the streamed end-to-end step, whose GEMMs run
+// beside the host-to-device copies, is faster (583 / 583 vs 537 / 537
+// TFLOP/s). Each CTA of a pair loads half of the B tile, so the kernel pulls
+// 2/3 of the single-CTA kernel's operand bytes from L2.
+// With fewer tiles the single-CTA kernel (and its split-K) keeps more SMs
+// busy. TTC_GEMM_PAIR=0 / 1 (read at every call) forces it off / on.
+bool use_pair(const ttc_gemm_desc& d, int sms) {
+    if (d.M < 2 * BM || d.N < P_BN) return false;
     const char* e = getenv("TTC_GEMM_PAIR");
-    return e && e[0] == '1' && d.M >= 2 * BM && d.N >= P_BN;
+    if (e && e[0] == '0') return false;
+    if (e && e[0] == '1') return true;
+    const long long pair_tiles = (long long)((d.M + 2 * BM - 1) / (2 * BM)) * ((d.N + P_BN - 1) / P_BN);
+    return pair_tiles >= sms / 2;
 }
 
 int launch_pair(TcParams& p) {
@@ -991,7 +999,7 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
                                       X3_SMEM_BYTES));
         attr_set = true;
     }
-    const bool pair = !x3 && use_pair(d);
+    const bool pair = !x3 && use_pair(d, rt().sm_count);
     const int bn = pair ? P_BNH : x3 ? X3_BN : BN;  // B columns one CTA loads per tile
     TcParams p;
     std::memset(&p, 0, sizeof p);
