@@ -164,6 +164,19 @@ def test_pipelined_plan_rebuilds_the_graph_over_row_chunks():
     assert len(tl.Plan([tl.all_reduce_sum(s)], pipeline_chunks=3)) == 8
 
 
+def test_pipelined_plan_over_a_resident_batch():
+    """With no streamed input, the batch is the one resident rank-2 constant
+    that is the matmuls' left operand; it is cut into constant row views (the
+    same tape shape as a streamed batch). Two such constants are ambiguous."""
+    xc = c((64, 16), 4)
+    W1, W2 = c((16, 32), 1), c((32, 8), 2)
+    s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(xc, W1)), W2)), [0])
+    assert len(tl.Plan([s], pipeline_chunks=4)) == 9
+    two = tl.reduce_sum(tl.add(tl.matmul(c((8, 16), 5), W1), tl.matmul(c((8, 16), 6), W1)), [0])
+    with pytest.raises(RuntimeError, match="streamed rank-2 batch input"):
+        tl.Plan([two], pipeline_chunks=2)
+
+
 def test_pipelined_plan_rejects_graphs_that_are_not_row_local():
     X = np.random.default_rng(0).standard_normal((64, 16)).astype(np.float32)
     xs = tl.streamed(X)

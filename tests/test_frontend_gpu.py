@@ -299,6 +299,29 @@ def test_pipelined_plan_matches_the_whole_batch_plan(chunks):
     assert np.allclose(piped.numpy(0), want, rtol=1e-5, atol=1e-5)
 
 
+def test_pipelined_plan_over_a_resident_batch_matches_the_whole_batch_plan():
+    """A resident batch (a constant) in 3 row chunks, on the TF32 path with
+    the CTA-pair GEMM where the chunk fills the GPU: the same column sums as
+    the whole-batch plan (up to the order of the partial sums) and, within
+    the TF32 bound, as the oracle."""
+    tl.set_gemm_path("auto")
+    rng = np.random.default_rng(32)
+    # a 2048-row chunk times W1 has 8 x 10 256x256 tiles: the CTA-pair kernel
+    X = rng.standard_normal((6144, 32)).astype(np.float32)
+    W1 = (rng.standard_normal((32, 2560)) / np.sqrt(32)).astype(np.float32)
+    W2 = (rng.standard_normal((2560, 64)) / np.sqrt(2560)).astype(np.float32)
+    s = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(tl.constant(X), tl.constant(W1))),
+                                           tl.constant(W2))), [0])
+    whole, piped = tl.Plan([s]), tl.Plan([s], pipeline_chunks=3)
+    whole.run()
+    for _ in range(2):
+        piped.run()
+        got = piped.numpy(0)
+        assert np.allclose(got, whole.numpy(0), rtol=1e-5, atol=0)
+    want = oracle.reduce(oracle.sigmoid(oracle.matmul(oracle.relu(oracle.matmul(X, W1)), W2)), (0,), f64=True)
+    assert normwise(got, want) <= 2e-3
+
+
 def test_large_mlp_at_full_size_on_sampled_rows():
     """The 65536 x 4096 -> 16384 -> 4096 MLP at its full size (TF32 tensor-core
     GEMMs, fused relu / sigmoid epilogues, batch column sums): sampled rows of
