@@ -162,6 +162,12 @@ def test_pipelined_plan_rebuilds_the_graph_over_row_chunks():
     assert len(tl.Plan([s], pipeline_chunks=4)) == 9
     # the all-reduce runs once, after the partial sums are combined
     assert len(tl.Plan([tl.all_reduce_sum(s)], pipeline_chunks=3)) == 8
+    # a streamed first chunk of 4096 rows or more is cut into 1/8, 1/8, 1/4 and 1/2 of it
+    # (5 row ranges here); a resident batch is not (no upload to wait for)
+    big = np.zeros((8192, 16), np.float32)
+    for x, n_ops in ((tl.streamed(big), 11), (tl.constant(big), 5)):
+        sb = tl.reduce_sum(tl.sigmoid(tl.matmul(tl.relu(tl.matmul(x, W1)), W2)), [0])
+        assert len(tl.Plan([sb], pipeline_chunks=2)) == n_ops
 
 
 def test_pipelined_plan_over_a_resident_batch():
