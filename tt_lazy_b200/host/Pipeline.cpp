@@ -144,7 +144,8 @@ void find_batch_input(const std::vector<Tensor>& outputs, Rebuilder& rb) {
                 rb.x_host = in.host_data();
                 rb.x_shape = in.shape_vector();
                 found = 1;
-            } else if (left_operand_op && i == 0 && in.rank() == 2 && in.host_data()) {
+            } else if (left_operand_op && i == 0 && in.rank() == 2 && in.is_constant() && in.host_data()) {
+                // a constant's caller-owned memory outlives the plan's row views of it
                 resident.insert({in.host_data(), in.shape_vector()});
             }
         }
