@@ -275,7 +275,10 @@ int ttc_copy2d(const float* in, int64_t in_ld, float* out, int64_t out_ld, int64
  * path: TTC_GEMM_FFMA -- fp32 CUDA-core FMA (norm-wise rel. error ~1e-6,
  *                         the 1e-5 bound);
  *       TTC_GEMM_TF32 -- tcgen05.mma kind::tf32, TMEM accumulators, TMA
- *                         operand loads (the 2e-3 bound);
+ *                         operand loads (the 2e-3 bound); a CTA pair
+ *                         (cta_group::2, 256x256 tiles) when those tiles
+ *                         number at least half the SMs, else one CTA per
+ *                         128x256 tile (split along K when tiles are few);
  *       TTC_GEMM_AUTO -- TF32 when the shape suits the tensor-core kernel,
  *                         else FFMA;
  *       TTC_GEMM_TF32X3 -- fp32-accurate products on the tensor cores: each
