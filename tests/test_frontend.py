@@ -181,6 +181,10 @@ def test_pipelined_plan_over_a_resident_batch():
     two = tl.reduce_sum(tl.add(tl.matmul(c((8, 16), 5), W1), tl.matmul(c((8, 16), 6), W1)), [0])
     with pytest.raises(RuntimeError, match="streamed rank-2 batch input"):
         tl.Plan([two], pipeline_chunks=2)
+    # a materialized tensor owns its storage, which the plan's row views would not keep alive
+    xm = tl.materialized(np.ones((64, 16), np.float32))
+    with pytest.raises(RuntimeError, match="streamed rank-2 batch input"):
+        tl.Plan([tl.reduce_sum(tl.matmul(xm, W1), [0])], pipeline_chunks=2)
 
 
 def test_pipelined_plan_rejects_graphs_that_are_not_row_local():
