@@ -73,7 +73,8 @@ def lib():
         L.orc_last_error.restype = C.c_char_p
         L.orc_relu.argtypes = [_f32p, _f32p, C.c_size_t]
         L.orc_sigmoid.argtypes = [_f32p, _f32p, C.c_size_t]
-        L.orc_sigmoid_cr.argtypes = [_f32p, _f32p, C.c_size_t]
+        L.orc_expf_ref.argtypes = [_f32p, _f32p, C.c_size_t]
+        L.orc_expf_libm.argtypes = [_f32p, _f32p, C.c_size_t]
         for fn in (L.orc_add, L.orc_multiply):
             fn.argtypes = [_f32p, _u32p, C.c_int, _f32p, _u32p, C.c_int, _f32p]
         L.orc_matmul.argtypes = [_f32p, C.c_uint32, C.c_uint32, _f32p, C.c_uint32, C.c_uint32,
@@ -129,12 +130,33 @@ def sigmoid(x):
     return out
 
 
-def sigmoid_cr(x):
-    """README sigmoid with a correctly rounded expf (see oracle.h)."""
+def expf_ref(x):
+    """glibc's expf restated as its x86-64 FMA build computes it (oracle.c)."""
     x = _f32(x)
     out = np.empty_like(x)
-    _chk(lib().orc_sigmoid_cr(x.reshape(-1), out.reshape(-1), x.size), lib())
+    _chk(lib().orc_expf_ref(x.reshape(-1), out.reshape(-1), x.size), lib())
     return out
+
+
+def expf_libm(x):
+    """This process's own expf (what the reference's std::exp(float) calls)."""
+    x = _f32(x)
+    out = np.empty_like(x)
+    _chk(lib().orc_expf_libm(x.reshape(-1), out.reshape(-1), x.size), lib())
+    return out
+
+
+def expf_is_fma_build() -> bool:
+    """True when this process's expf is glibc's FMA build. The device sigmoid
+    equals the reference's on every float then; with glibc's other x86-64
+    build one float of sigmoid differs by 1 ulp."""
+    return bool(lib().orc_expf_is_fma_build())
+
+
+def sigmoid_ulp_bound() -> int:
+    """Largest ulp distance the tests allow between the device sigmoid and
+    sigmoid() on this host: 0 where the host's expf is glibc's FMA build."""
+    return 0 if expf_is_fma_build() else 1
 
 
 def _binary(fn, a, b):

@@ -54,16 +54,73 @@ int orc_sigmoid(const float* x, float* out, size_t n) {
     return 0;
 }
 
-/* The same formula with e^-x correctly rounded to float (glibc's expf is
- * within 0.502 ulp, so it differs from this by 1 ulp on ~0.07% of inputs):
- * double exp is accurate to ~1 ulp of double, so one rounding to float is
- * the correctly rounded result except within 2^-52 of a float midpoint. */
-int orc_sigmoid_cr(const float* x, float* out, size_t n) {
-    for (size_t i = 0; i < n; ++i) {
-        const float e = (float)exp(-(double)x[i]);
-        out[i] = 1.0f / (1.0f + e);
+/* glibc's expf as its x86-64 FMA build computes it (glibc 2.27+,
+ * sysdeps/ieee754/flt-32/e_expf.c compiled with FMA contraction, the build
+ * selected on hosts with AVX2 and FMA): a restatement of the published
+ * method, used to pin what the reference's std::exp(float) returns. The
+ * tests compare it with this process's expf on a sweep of floats and report
+ * which glibc build the host runs (orc_expf_is_fma_build). */
+/* 2^(j/32) rounded to double. */
+static const double g_exp2_32[32] = {
+    0x1.0000000000000p+0, 0x1.059b0d3158574p+0, 0x1.0b5586cf9890fp+0, 0x1.11301d0125b51p+0,
+    0x1.172b83c7d517bp+0, 0x1.1d4873168b9aap+0, 0x1.2387a6e756238p+0, 0x1.29e9df51fdee1p+0,
+    0x1.306fe0a31b715p+0, 0x1.371a7373aa9cbp+0, 0x1.3dea64c123422p+0, 0x1.44e086061892dp+0,
+    0x1.4bfdad5362a27p+0, 0x1.5342b569d4f82p+0, 0x1.5ab07dd485429p+0, 0x1.6247eb03a5585p+0,
+    0x1.6a09e667f3bcdp+0, 0x1.71f75e8ec5f74p+0, 0x1.7a11473eb0187p+0, 0x1.82589994cce13p+0,
+    0x1.8ace5422aa0dbp+0, 0x1.93737b0cdc5e5p+0, 0x1.9c49182a3f090p+0, 0x1.a5503b23e255dp+0,
+    0x1.ae89f995ad3adp+0, 0x1.b7f76f2fb5e47p+0, 0x1.c199bdd85529cp+0, 0x1.cb720dcef9069p+0,
+    0x1.d5818dcfba487p+0, 0x1.dfc97337b9b5fp+0, 0x1.ea4afa2a490dap+0, 0x1.f50765b6e4540p+0,
+};
+
+static float expf_glibc_fma(float x) {
+    uint32_t ux;
+    memcpy(&ux, &x, 4);
+    const uint32_t abstop = (ux >> 20) & 0x7ff;
+    if (abstop >= 0x42b) { /* |x| >= 88 or NaN */
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8) return x + x;
+        if (x > 0x1.62e42ep6f) return INFINITY;
+        if (x < -0x1.9fe368p6f) return 0.0f;
     }
+    const double xd = x, inv_ln2_n = 0x1.71547652b82fep+5, shift = 0x1.8p+52;
+    double kd = fma(inv_ln2_n, xd, shift);
+    uint64_t ki;
+    memcpy(&ki, &kd, 8);
+    kd -= shift;
+    const double r = fma(inv_ln2_n, xd, -kd);
+    uint64_t t;
+    memcpy(&t, &g_exp2_32[ki % 32], 8);
+    t += (ki - ki % 32) << 47; /* exponent: (k >> 5) << 52 */
+    double s;
+    memcpy(&s, &t, 8);
+    const double z = fma(0x1.c6af84b912394p-20, r, 0x1.ebfce50fac4f3p-13);
+    const double r2 = r * r;
+    double y = fma(0x1.62e42ff0c52d6p-6, r, 1.0);
+    y = fma(z, r2, y);
+    return (float)(y * s);
+}
+
+int orc_expf_ref(const float* x, float* out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = expf_glibc_fma(x[i]);
     return 0;
+}
+
+int orc_expf_libm(const float* x, float* out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = expf(x[i]);
+    return 0;
+}
+
+/* 1 when this process's expf is glibc's FMA build: the two x86-64 builds
+ * differ at x = 0x1.04845ep+5 (the FMA build returns 0x1.f93e38p+46). */
+int orc_expf_is_fma_build(void) {
+    volatile float probe = 0x1.04845ep+5f;
+    const float e = expf(probe);
+    uint32_t u;
+    memcpy(&u, &e, 4);
+    const float want = 0x1.f93e38p+46f;
+    uint32_t w;
+    memcpy(&w, &want, 4);
+    return u == w;
 }
 
 /* Broadcast compatibility of eltwise.cpp:40-42 (Tensor::can_broadcast,

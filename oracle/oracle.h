@@ -34,9 +34,12 @@ int orc_relu(const float* x, float* out, size_t n);
 /* README.md:332 -- 1.0f / (1.0f + std::exp(-x)); std::exp(float) is expf. */
 int orc_sigmoid(const float* x, float* out, size_t n);
 
-/* README.md:332 with e^-x correctly rounded (float)exp((double)-x): the
- * formula's value independent of the libm's expf rounding. */
-int orc_sigmoid_cr(const float* x, float* out, size_t n);
+/* glibc's expf, restated as its x86-64 FMA build computes it, and the
+ * process's own expf (libm); orc_expf_is_fma_build reports whether the
+ * process's expf is that build. */
+int orc_expf_ref(const float* x, float* out, size_t n);
+int orc_expf_libm(const float* x, float* out, size_t n);
+int orc_expf_is_fma_build(void);
 
 /* src/backend/cpu/eltwise.cpp:29-83 -- same-shape add, or [N,M] + [1,M]. */
 int orc_add(const float* a, const uint32_t* ashape, int arank,

@@ -11,10 +11,11 @@ with the specialised kernels off, where the large layouts take the
 TMA-staged interpreter.
 
 Bounds, as in the other parity tests: stored results are bit-exact against
-the oracle's IEEE float32 steps when the program has no sigmoid (sigmoid is
-within 1 ulp of the correctly rounded formula, so programs with one get a
-few ulps after later steps); reductions are within 1e-5 of the fp64 sum of
-the oracle's own element values, relative to the sum of magnitudes.
+the oracle's IEEE float32 steps, sigmoid included (it returns the
+reference formula's float; on a host whose glibc is its build without FMA,
+one float of sigmoid is 1 ulp away, and programs with a sigmoid then get a
+1e-5 relative bound); reductions are within 1e-5 of the fp64 sum of the
+oracle's own element values, relative to the sum of magnitudes.
 """
 import os
 import subprocess
@@ -74,7 +75,7 @@ def _evaluate(prog, xs):
         elif op == "RELU":
             acc = oracle.relu(acc)
         elif op == "SIGMOID":
-            acc = oracle.sigmoid_cr(acc)
+            acc = oracle.sigmoid(acc)
         elif op in ("ADD", "MUL"):
             other = acc if src == "ACC" else xs[idx] if src == "INPUT" else slots[idx]
             acc = (acc + other) if op == "ADD" else (acc * other)
@@ -128,7 +129,9 @@ def test_random_chain_matches_oracle(ttc, seed):
     ttc.eltwise_chain(desc)
 
     acc, want_outs = _evaluate(prog, host)
-    has_sigmoid = any(op == "SIGMOID" for op, _, _ in prog)
+    # sigmoid is exact against this host's formula unless its glibc is the
+    # build without FMA (oracle.sigmoid_ulp_bound)
+    has_sigmoid = any(op == "SIGMOID" for op, _, _ in prog) and oracle.sigmoid_ulp_bound() > 0
     for i in range(n_out):
         got, want = outs[i].numpy(), want_outs[i]
         both_nan = np.isnan(got) & np.isnan(want)

@@ -94,7 +94,7 @@ def test_random_gemm_matches_oracle(ttc, seed):
         elif step == "relu":
             y = oracle.relu(y)
         elif step == "sigmoid":
-            y = oracle.sigmoid_cr(y)
+            y = oracle.sigmoid(y)
         else:
             stored.append(y.copy())
     tol = TOL[path]

@@ -125,3 +125,24 @@ def test_against_live_reference():
     y = oracle.relu(x)
     z = oracle.add(y, y)
     assert np.array_equal(R.lazy_chain(x), oracle.multiply(z, z))
+
+
+def test_expf_restatement_pinned_to_libm():
+    """oracle.expf_ref (glibc's expf as its FMA build computes it) against this
+    process's expf on every 61st bit pattern and the specials; on a host whose
+    glibc picks that build they agree everywhere (the host test of the device
+    header checks all 2^32 floats)."""
+    u = np.arange(0, 1 << 32, 61, dtype=np.uint64).astype(np.uint32)
+    x = np.concatenate([u.view(np.float32), np.array([np.inf, -np.inf, np.nan, 88.0, -88.0] + [float.fromhex(h) for h in (
+        "0x1.62e42ep6", "-0x1.9fe368p6", "0x1.04845ep+5", "-0x1.f8cbb2p+5")], np.float32)])
+    a, b = oracle.expf_ref(x), oracle.expf_libm(x)
+    diff = (a.view(np.int32) != b.view(np.int32)) & ~(np.isnan(a) & np.isnan(b))
+    if oracle.expf_is_fma_build():
+        assert not diff.any(), x[diff][:8]
+    else:
+        assert diff.sum() <= 2
+    # the reference formula through libm equals the restatement's sigmoid
+    xs = x[np.abs(x) < 200]
+    want = (np.float32(1) / (np.float32(1) + oracle.expf_ref(-xs))).astype(np.float32)
+    got = oracle.sigmoid(xs)
+    assert np.sum(got.view(np.int32) != want.view(np.int32)) <= oracle.sigmoid_ulp_bound()

@@ -72,9 +72,9 @@ def _headers(*dirs):
 
 
 def _embed_jit_source():
-    """exp_cr.cuh + chain_jit_device.cuh as a C++ raw string (the NVRTC
+    """expf_ref.cuh + chain_jit_device.cuh as a C++ raw string (the NVRTC
     source prefix; NVRTC gets no include path)."""
-    srcs = [os.path.join(CSRC, "exp_cr.cuh"), os.path.join(CSRC, "chain_jit_device.cuh")]
+    srcs = [os.path.join(CSRC, "expf_ref.cuh"), os.path.join(CSRC, "chain_jit_device.cuh")]
     out = os.path.join(OBJ, "chain_jit_src.inc")
     if _stale(out, srcs):
         text = "\n".join(line for s in srcs for line in open(s).read().splitlines()

@@ -45,7 +45,7 @@ struct JParams {
 #if defined(__CUDACC_RTC__) || defined(__CUDA_ARCH__)
 
 #ifndef __CUDACC_RTC__
-#include "exp_cr.cuh"
+#include "expf_ref.cuh"
 #endif
 
 #define TTJ_THREADS 256
@@ -54,15 +54,15 @@ __device__ __forceinline__ unsigned ttj_fdiv(unsigned n, const JFastDiv& f) { re
 
 __device__ __forceinline__ float ttj_relu(float x) { return (0.0f < x) ? x : 0.0f; }
 
-// sigmoid with the exp of exp_cr.cuh (NVRTC receives that file's text ahead
+// sigmoid with the exp of expf_ref.cuh (NVRTC receives that file's text ahead
 // of this one): one range test for all G*W values of a thread.
-__shared__ ExpCrTable ttj_exp_tab;
+__shared__ ExpTable ttj_exp_tab;
 
-__device__ __forceinline__ void ttj_exp_table_init() { exp_cr_table_init(ttj_exp_tab); }
+__device__ __forceinline__ void ttj_exp_table_init() { exp_table_init(ttj_exp_tab); }
 
 template <int G, int W>
 __device__ __forceinline__ void ttj_sigmoid_all(float (&acc)[G][W]) {
-    sigmoid_cr_n<G * W>(&acc[0][0], ttj_exp_tab);
+    sigmoid_ref_n<G * W>(&acc[0][0], ttj_exp_tab);
 }
 
 // Operand kinds: 0 full (contiguous columns), 1 row broadcast ([1,C]),

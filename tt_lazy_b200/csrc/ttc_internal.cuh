@@ -10,7 +10,7 @@
 
 #include "../../include/tt_cuda.h"
 #ifdef __CUDACC__
-#include "exp_cr.cuh"
+#include "expf_ref.cuh"
 #endif
 
 // ------------------------------------------------------------------ errors
@@ -164,12 +164,12 @@ __device__ __forceinline__ void store_group(const DOutView& v, long long seg, lo
 
 __device__ __forceinline__ float op_relu(float x) { return (0.0f < x) ? x : 0.0f; }
 
-// sigmoid = 1 / (1 + e^-x) with the exp of exp_cr.cuh; its 2^(j/64) table
+// sigmoid = 1 / (1 + e^-x) with the exp of expf_ref.cuh; its 32-entry table
 // lives in shared memory (exp2_table_init_block fills it at kernel start,
 // before a __syncthreads).
-static __shared__ ExpCrTable s_exp_tab;
+static __shared__ ExpTable s_exp_tab;
 
-__device__ __forceinline__ void exp2_table_init_block() { exp_cr_table_init(s_exp_tab); }
+__device__ __forceinline__ void exp2_table_init_block() { exp_table_init(s_exp_tab); }
 
 // Applies f(g, w) to every element. Arithmetic runs on all groups (invalid
 // groups compute on zeros and are never stored or summed).
@@ -220,7 +220,7 @@ __device__ __forceinline__ void run_program_io(const DProgram& P, float (&acc)[G
             case D_RELU: each<G, W>([&](int g, int w) { acc[g][w] = op_relu(acc[g][w]); }); break;
             case D_SIGMOID:
 #pragma unroll
-                for (int g = 0; g < G; ++g) sigmoid_cr_n<W>(acc[g], s_exp_tab);
+                for (int g = 0; g < G; ++g) sigmoid_ref_n<W>(acc[g], s_exp_tab);
                 break;
             case D_ADD_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] + acc[g][w]; }); break;
             case D_MUL_ACC: each<G, W>([&](int g, int w) { acc[g][w] = acc[g][w] * acc[g][w]; }); break;

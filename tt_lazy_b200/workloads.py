@@ -10,7 +10,10 @@ front end (the same calls a user makes):
 - ``dag_stress``: a random DAG of ``nodes`` operations (seed 4) over
   [n, n] tensors mixing matmul / relu / sigmoid / add / multiply, with
   reduce_sum at the sinks and ``dead_frac`` of the operations unreachable
-  from the outputs (tape build, dead-code elimination and fusion under load).
+  from the outputs (tape build, dead-code elimination and fusion under load);
+  ``dag_stress_program`` draws its data and topology and ``dag_build``
+  creates the graph nodes, so the two can be timed apart and the program
+  replayed on the oracle.
 
 Inputs are seeded synthetic data with the workloads' shapes and
 distributions. Each builder returns the lazy outputs plus a description of
@@ -53,55 +56,89 @@ def small_mlp(seed: int = 1, batch: int = 256, d_in: int = 512, d_hidden: int = 
     return m, work
 
 
-def dag_stress(n: int = 4096, nodes: int = 200, seed: int = 4, dead_frac: float = 0.4, sinks: int = 4):
-    """(outputs, work): a random DAG of `nodes` operations over [n, n].
+def dag_stress_program(n: int = 4096, nodes: int = 200, seed: int = 4, dead_frac: float = 0.4, sinks: int = 4):
+    """(inputs, program, work): the data and topology of the DCE / fusion
+    stress graph, before any graph node exists.
 
+    inputs: x0 [n, n] ~ U(-1, 1), two weights N(0, 1/n), two gates U(-1, 1).
+    program: one (kind, a, b) per operation, operands numbered as values:
+    0 = x0, 1 + i = operation i; b names a weight (matmul), a second value
+    (add) or a gate / earlier sigmoid (multiply: "g0", "g1" or a value).
     The live part is a chain in which operation i always reads operation
     i - 1 (so every live operation reaches the last one) plus a second,
     random earlier operand for the binary ops; the dead part reads live or
     dead operations but feeds nothing. reduce_sum(dim 1) is taken at the last
     `sinks` live operations. Magnitudes stay bounded: matmul's right operand
     is a constant N(0, 1/n) matrix, multiply's second operand a constant in
-    [-1, 1] or a sigmoid output, so only add grows values (by at most 2x)."""
+    [-1, 1] or a sigmoid output, so only add grows values (by at most 2x).
+    Every operation is row-local (matmul has a constant on the right), so
+    row r of any value depends only on row r of x0 and of the gates."""
     rng = np.random.default_rng(seed)
     n_dead = int(round(nodes * dead_frac))
     n_live = nodes - n_dead
-    x0 = tl.constant(rng.uniform(-1, 1, (n, n)).astype(np.float32))
-    weights = [tl.constant((rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float32)) for _ in range(2)]
-    gates = [tl.constant(rng.uniform(-1, 1, (n, n)).astype(np.float32)) for _ in range(2)]
+    inputs = {"x0": rng.uniform(-1, 1, (n, n)).astype(np.float32)}
+    for i in range(2):
+        inputs[f"w{i}"] = (rng.standard_normal((n, n)) / np.sqrt(n)).astype(np.float32)
+    for i in range(2):
+        inputs[f"g{i}"] = rng.uniform(-1, 1, (n, n)).astype(np.float32)
     kinds = ["matmul", "relu", "sigmoid", "add", "multiply"]
     counts = dict.fromkeys(kinds, 0)
-    sig_ids: list[int] = []
+    program: list[tuple] = []
+    sig_vals: list[int] = []
 
-    def make(prev, pool, kind):
+    def op(kind, prev, pool):
         if kind == "matmul":
-            return tl.matmul(prev, weights[int(rng.integers(0, 2))])
-        if kind == "relu":
-            return tl.relu(prev)
-        if kind == "sigmoid":
-            return tl.sigmoid(prev)
+            return (kind, prev, f"w{int(rng.integers(0, 2))}")
+        if kind in ("relu", "sigmoid"):
+            return (kind, prev, None)
         if kind == "add":
-            return tl.add(prev, pool[int(rng.integers(0, len(pool)))])
-        # multiply by a bounded operand: a constant gate or an earlier sigmoid
-        bounded = [gates[0], gates[1]] + [pool[i] for i in sig_ids if i < len(pool)]
-        return tl.multiply(prev, bounded[int(rng.integers(0, len(bounded)))])
+            return (kind, prev, pool[int(rng.integers(0, len(pool)))])
+        bounded = ["g0", "g1"] + [v for v in sig_vals if v < len(pool)]
+        return (kind, prev, bounded[int(rng.integers(0, len(bounded)))])
 
-    live = [x0]
+    live = [0]
     for _ in range(n_live):
         kind = kinds[int(rng.integers(0, len(kinds)))]
         counts[kind] += 1
-        live.append(make(live[-1], live, kind))
+        program.append(op(kind, live[-1], live))
+        live.append(len(program))
         if kind == "sigmoid":
-            sig_ids.append(len(live) - 1)
-    dead = []
+            sig_vals.append(len(live) - 1)
+    dead: list[int] = []
     for _ in range(n_dead):
         kind = kinds[int(rng.integers(0, len(kinds)))]
         src = live + dead
-        dead.append(make(src[int(rng.integers(0, len(src)))], src, kind))
-    outs = [tl.reduce_sum(t, [1]) for t in live[-sinks:]]
+        program.append(op(kind, src[int(rng.integers(0, len(src)))], src))
+        dead.append(len(program))
+    sink_vals = live[-sinks:]
     elem = 4 * n * n
     bytes_live = (counts["relu"] + counts["sigmoid"]) * 2 * elem + (counts["add"] + counts["multiply"]) * 3 * elem
     bytes_live += counts["matmul"] * 3 * elem + sinks * (elem + 4 * n)
     work = {"flops": counts["matmul"] * 2 * n ** 3, "bytes_unfused": bytes_live, "live_ops": n_live + sinks,
-            "dead_ops": n_dead, "graph_nodes": nodes + sinks, "counts": counts}
-    return outs, work
+            "dead_ops": n_dead, "graph_nodes": nodes + sinks, "counts": counts, "sinks": sink_vals}
+    return inputs, program, work
+
+
+def dag_build(inputs: dict, program: list, sinks: list):
+    """The lazy graph of a stress program: constants, one front-end call per
+    operation, reduce_sum(dim 1) at the sink values. Returns the outputs."""
+    const = {k: tl.constant(v) for k, v in inputs.items()}
+    vals = [const["x0"]]
+    for kind, a, b in program:
+        if kind == "matmul":
+            vals.append(tl.matmul(vals[a], const[b]))
+        elif kind == "relu":
+            vals.append(tl.relu(vals[a]))
+        elif kind == "sigmoid":
+            vals.append(tl.sigmoid(vals[a]))
+        elif kind == "add":
+            vals.append(tl.add(vals[a], vals[b]))
+        else:
+            vals.append(tl.multiply(vals[a], const[b] if isinstance(b, str) else vals[b]))
+    return [tl.reduce_sum(vals[s], [1]) for s in sinks]
+
+
+def dag_stress(n: int = 4096, nodes: int = 200, seed: int = 4, dead_frac: float = 0.4, sinks: int = 4):
+    """(outputs, work): the stress graph built through the front end."""
+    inputs, program, work = dag_stress_program(n, nodes, seed, dead_frac, sinks)
+    return dag_build(inputs, program, work["sinks"]), work
