@@ -215,10 +215,15 @@ int ttc_eltwise_chain(const ttc_chain_desc* desc);
  * It calls no cudaMalloc, cudaFree or allocating library routine: the
  * per-block partial sums of a reduction go to a fixed 1 MiB device array
  * compiled into the library (every GPU that loads the library holds it until
- * the process exits). A reduction that would need more partials than fit
- * returns TTC_ERR_INVALID_ARGUMENT with the sizes in ttc_last_error(). The
+ * the process exits). The launch sizes its grid so the partials fit: a full
+ * sum uses at most 262144 / nseg blocks per segment, a column sum at most
+ * 262144 / (nseg x cols) row bands (one band needs no partials), so every
+ * descriptor ttc_eltwise_chain accepts runs here too, with fewer blocks when
+ * the array is the limit. A launch whose partials would still not fit
+ * returns TTC_ERR_INVALID_ARGUMENT with both sizes in ttc_last_error(). The
  * first call on a device looks up that array's device address (with the
- * library's device current); make that first call before any stream capture.
+ * library's device current; first calls from several threads wait for one
+ * lookup); make that first call before any stream capture.
  * All calls share the one array and it keeps the last call's contents (the
  * kernels overwrite every partial they read, nothing needs clearing), so
  * calls that overlap on the GPU -- on different streams, or from different

@@ -50,7 +50,9 @@ def build(force: bool = False) -> str:
 
 def build_ref(force: bool = False) -> str | None:
     """Compile the reference sources into _ref/libttref.so when they are present."""
-    ref_root = os.environ.get("TT_REFERENCE_ROOT", "/root/reference")
+    # the reference checkout: $TT_REFERENCE_ROOT, default "reference" beside this repository
+    ref_root = os.environ.get("TT_REFERENCE_ROOT",
+                              os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
     deps = [os.path.join(HERE, "ref_capi.cpp"), os.path.join(HERE, "build_ref.sh")]
     if not os.path.isdir(os.path.join(ref_root, "src", "backend", "cpu")):
         return REF_SO if os.path.exists(REF_SO) else None

@@ -7,8 +7,10 @@
 # this image); the same release flags (-O3 -DNDEBUG, CMakeLists.txt:116) are.
 # spdlog is header-only and comes from the copy bundled with flashinfer.
 set -e
-REF=${TT_REFERENCE_ROOT:-/root/reference}
 HERE=$(cd "$(dirname "$0")" && pwd)
+# the reference checkout: $TT_REFERENCE_ROOT, default a directory named
+# "reference" beside this repository
+REF=${TT_REFERENCE_ROOT:-$(cd "$HERE/../.." && pwd)/reference}
 OUT="$HERE/_ref"
 if [ ! -d "$REF/src/backend/cpu" ]; then
     echo "build_ref.sh: reference sources not found at $REF; skipping" >&2

@@ -1,9 +1,10 @@
-"""Small, self-contained launches of the hot kernels for profiling.
+"""Small, self-contained launches of the hot kernels for profiling (the
+cases the ncu summaries under profiles/ were captured on; not a test module).
 
-    python -m tt_lazy_b200.prof gemm [M] [tf32|tf32x3|ffma]  # the GEMM path's kernel: X[M,4096] . W[4096,16384], 3 launches
-    python -m tt_lazy_b200.prof chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
-    python -m tt_lazy_b200.prof small_mlp      # the small MLP workload through tl.Plan, 3 runs
-    python -m tt_lazy_b200.prof transpose [N]  # transpose_kernel on an N x N fp32 input, 3 launches
+    python tests/profile_cases.py gemm [M] [tf32|tf32x3|ffma]  # the GEMM path's kernel: X[M,4096] . W[4096,16384], 3 launches
+    python tests/profile_cases.py chain NAME [N] # one chain kernel on an N x N fp32 input, 3 launches
+    python tests/profile_cases.py small_mlp      # the small MLP workload through tl.Plan, 3 runs
+    python tests/profile_cases.py transpose [N]  # transpose_kernel on an N x N fp32 input, 3 launches
 
 NAME: copy | readme (relu -> add -> multiply, stored, summed) | sigmoid |
 segments (sigmoid(C) * relu(C + C) over 8 row segments, column sums).
@@ -12,7 +13,10 @@ nothing is timed here (profile with ncu, time with bench.py).
 """
 from __future__ import annotations
 
+import os
 import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
 
 def _setup():

@@ -36,6 +36,7 @@ clear = _fe.clear
 clear_cache = _fe.clear_cache
 tape = _fe.tape
 stats = _fe.stats
+reset_peak = _fe.reset_peak
 graph_size = _fe.graph_size
 set_optimization = _fe.set_optimization
 synchronize = _fe.synchronize

@@ -12,7 +12,9 @@
 // op, as in the reference's separate passes.
 #include <algorithm>
 #include <cstdlib>
+#include <atomic>
 #include <cstring>
+#include <mutex>
 
 #include "tma_util.cuh"
 
@@ -224,6 +226,17 @@ int occupancy_grid(K kernel) {
     return per_sm * rt().sm_count;
 }
 
+// occupancy_grid of `kernel`, queried once per device into the call site's
+// own cache (kernels of one signature share a function-pointer type, so the
+// cache cannot be keyed by type).
+template <class K>
+int occupancy_grid_cached(int (&cache)[kMaxDevices], K kernel) {
+    const int dev = rt().device;
+    if (dev < 0 || dev >= kMaxDevices) return occupancy_grid(kernel);
+    if (cache[dev] < 1) cache[dev] = occupancy_grid(kernel);
+    return cache[dev];
+}
+
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
 
 // 128-bit path precondition: every contiguous operand starts on 16 bytes and
@@ -267,7 +280,8 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p, const FixedScratch* fi
     switch (d.reduce) {
         case TTC_REDUCE_NONE: {
             const long long need = ((long long)p.total + kThreads * kGroups - 1) / (kThreads * kGroups);
-            static int cap = occupancy_grid(chain_flat_kernel<W, false>);
+            static int cap_cache[kMaxDevices] = {};
+            const int cap = occupancy_grid_cached(cap_cache, chain_flat_kernel<W, false>);
             const int gx = (int)std::max<long long>(1, std::min<long long>(need, std::max(1, cap / nseg)));
             chain_flat_kernel<W, false><<<dim3(gx, nseg), kThreads, 0, st>>>(p);
             count_launch();
@@ -275,8 +289,12 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p, const FixedScratch* fi
         }
         case TTC_REDUCE_ALL: {
             const long long need = ((long long)p.total + kThreads * kGroups - 1) / (kThreads * kGroups);
-            static int cap = occupancy_grid(chain_flat_kernel<W, true>);
-            const int gx = (int)std::max<long long>(1, std::min<long long>(need, std::max(1, cap / nseg)));
+            static int cap_cache[kMaxDevices] = {};
+            const int cap = occupancy_grid_cached(cap_cache, chain_flat_kernel<W, true>);
+            long long gx_max = std::max(1, cap / nseg);
+            // a fixed scratch array bounds the partials: fewer blocks, each over more tiles
+            if (fixed) gx_max = std::min<long long>(gx_max, std::max<long long>(1, (long long)fixed->floats / nseg));
+            const int gx = (int)std::max<long long>(1, std::min<long long>(need, gx_max));
             void* ws = nullptr;
             if (int rc = scratch_for((size_t)gx * nseg, fixed, &ws)) return rc;
             p.partials = (float*)ws;
@@ -286,7 +304,8 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p, const FixedScratch* fi
             break;
         }
         case TTC_REDUCE_ROWS: {
-            static int cap = occupancy_grid(chain_rows_kernel<W>);
+            static int cap_cache[kMaxDevices] = {};
+            const int cap = occupancy_grid_cached(cap_cache, chain_rows_kernel<W>);
             const long long need = ((long long)p.rows + (kThreads / 32) - 1) / (kThreads / 32);
             const int gx = (int)std::max<long long>(1, std::min<long long>(need, std::max(1, cap / nseg)));
             chain_rows_kernel<W><<<dim3(gx, nseg), kThreads, 0, st>>>(p);
@@ -294,10 +313,15 @@ int launch_chain(const ttc_chain_desc& d, ChainParams& p, const FixedScratch* fi
             break;
         }
         case TTC_REDUCE_COLS: {
-            static int cap = occupancy_grid(chain_cols_kernel<W>);
+            static int cap_cache[kMaxDevices] = {};
+            const int cap = occupancy_grid_cached(cap_cache, chain_cols_kernel<W>);
             const int gx = (int)((p.cpr + 31) / 32);
             const long long base = (long long)gx * nseg;
             int nsplit = (int)std::min<long long>((cap + base - 1) / base, (p.rows + 63) / 64);
+            // a fixed scratch array bounds the partials (nsplit x nseg x cols):
+            // fewer, longer row bands; one band needs no partials at all
+            if (fixed)
+                nsplit = (int)std::min<long long>(nsplit, (long long)fixed->floats / ((long long)nseg * p.cols));
             nsplit = std::max(nsplit, 1);
             p.rows_per_split = (p.rows + nsplit - 1) / nsplit;
             nsplit = (p.rows + p.rows_per_split - 1) / p.rows_per_split;
@@ -542,8 +566,8 @@ int ttc_reduce(const float* in, const uint32_t* shape, int rank, const int32_t* 
 namespace {
 constexpr size_t kNoAllocScratchFloats = 262144;  // 1 MiB; every GPU that loads the library holds it
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
-constexpr int kMaxDevices = 64;
-float* g_noalloc_scratch_dev[kMaxDevices] = {};  // device address of the array, per device
+std::mutex g_noalloc_mu;                                   // serialises the first-call address lookup
+std::atomic<float*> g_noalloc_scratch_dev[kMaxDevices] = {};  // device address of the array, per device
 }  // namespace
 
 extern "C" int ttc_eltwise_chain_noalloc(const ttc_chain_desc* desc) {
@@ -551,18 +575,26 @@ extern "C" int ttc_eltwise_chain_noalloc(const ttc_chain_desc* desc) {
     if (!desc) return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: desc is NULL");
     const int dev = rt().device;
     if (dev < 0 || dev >= kMaxDevices) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: device %d", dev);
-    if (!g_noalloc_scratch_dev[dev]) {
+    float* scratch = g_noalloc_scratch_dev[dev].load(std::memory_order_acquire);
+    if (!scratch) {
         // First call on this device: the host-side name of the array is not a
-        // device address, so look the address up once with the device current.
-        int cur = -1;
-        TTC_CUDA(cudaGetDevice(&cur));
-        if (cur != dev)
-            return set_error(TTC_ERR_INVALID_ARGUMENT,
-                             "tt_cuda: current device %d is not the library's device %d", cur, dev);
-        void* p = nullptr;
-        TTC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-        g_noalloc_scratch_dev[dev] = static_cast<float*>(p);
+        // device address, so look the address up once with the device
+        // current. Threads making their first call at the same time wait for
+        // one lookup.
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        scratch = g_noalloc_scratch_dev[dev].load(std::memory_order_relaxed);
+        if (!scratch) {
+            int cur = -1;
+            TTC_CUDA(cudaGetDevice(&cur));
+            if (cur != dev)
+                return set_error(TTC_ERR_INVALID_ARGUMENT,
+                                 "tt_cuda: current device %d is not the library's device %d", cur, dev);
+            void* p = nullptr;
+            TTC_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            scratch = static_cast<float*>(p);
+            g_noalloc_scratch_dev[dev].store(scratch, std::memory_order_release);
+        }
     }
-    const FixedScratch fixed{g_noalloc_scratch_dev[dev], kNoAllocScratchFloats};
+    const FixedScratch fixed{scratch, kNoAllocScratchFloats};
     return run_chain_impl(*desc, &fixed);
 }

@@ -56,6 +56,8 @@ struct Params {
     int mean;
     double count;
     int* status;
+    long long wait_limit;  // cycles a bounded wait spins before it gives up
+    int stall;             // failure-detection test: the producer issues no loads
 };
 
 template <int G>
@@ -151,11 +153,11 @@ __global__ void __launch_bounds__(kThreads, 1) chain_staged_kernel(const __grid_
             uint32_t phase = 0;
             long long issued = 0;
             bool failed = false;
-            for (unsigned i = blockIdx.x; i < p.n_items && !failed; i += gridDim.x) {
+            for (unsigned i = blockIdx.x; i < p.n_items && !failed && !p.stall; i += gridDim.x) {
                 const Item it = item_of(p, i);
                 for (int r = 0; r < it.nrt && !failed; ++r) {
                     for (int c = 0; c < it.nct; ++c) {
-                        if (!mbar_wait(empty_bar(stage), phase ^ 1)) {
+                        if (!mbar_wait(empty_bar(stage), phase ^ 1, p.wait_limit)) {
                             failed = true;
                             break;
                         }
@@ -182,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_staged_kernel(const __grid_
             const long long last = issued < p.stages ? issued : p.stages;
             for (long long j = 0; j < last; ++j) {
                 const long long n = issued - 1 - j;
-                if (!mbar_wait(full_bar((int)(n % p.stages)), (uint32_t)((n / p.stages) & 1))) failed = true;
+                if (!mbar_wait(full_bar((int)(n % p.stages)), (uint32_t)((n / p.stages) & 1), p.wait_limit)) failed = true;
             }
             if (failed) *(volatile int*)p.status = 1;
         }
@@ -208,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_staged_kernel(const __grid_
         for (int g = 0; g < G; ++g) rsum[g] = 0.0f;
         for (int r = 0; r < it.nrt; ++r) {
             for (int c = 0; c < it.nct; ++c) {
-                if (!failed) failed = !__all_sync(0xffffffffu, mbar_wait(full_bar(stage), phase));
+                if (!failed) failed = !__all_sync(0xffffffffu, mbar_wait(full_bar(stage), phase, p.wait_limit));
                 if (!failed) {
                     long long row[G], col[G];
                     bool valid[G];
@@ -302,7 +304,10 @@ bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15) == 0; }
 
 template <int G, int NS>
 void set_smem_attr() {
-    static bool done = false;
+    static bool done_by_dev[kMaxDevices] = {};
+    const int dev = rt().device;
+    if (dev < 0 || dev >= kMaxDevices) return;  // run_chain_impl's device check rejects these first
+    bool& done = done_by_dev[dev];
     if (!done) {
         cudaFuncSetAttribute(chain_staged_kernel<G, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              1024 + kSmemBudget + 2 * kMaxStages * 8 + 8 * kConsumers * 4);
@@ -373,6 +378,8 @@ int launch_chain_tma(const ttc_chain_desc& d, const DProgram& prog, bool* launch
               : d.reduce == TTC_REDUCE_COLS ? (double)d.rows
                                              : (double)d.rows * d.cols;
     if (int rc = device_status_ptr(&p.status)) return rc;
+    p.stall = stall_test("chain") ? 1 : 0;
+    p.wait_limit = p.stall ? kStallTestLimitCycles : kWaitLimitCycles;
     const int sms = rt().sm_count;
     p.nsplit = 1;
     p.split_tiles = p.tiles_r;

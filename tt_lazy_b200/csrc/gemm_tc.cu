@@ -22,8 +22,11 @@
 // The tile order is grouped by 16 row-blocks so the A and B panels a wave of
 // CTAs touches stay in the 126 MB L2.
 //
-// No TMA multicast and no clusters: the kernel is also used by every rank of
-// a multi-GPU run. Every mbarrier wait is bounded (about 2 s); an expired
+// The CTA-pair kernel below (tcgen05.mma.cta_group::2) runs as clusters of
+// 2; the single-CTA kernels launch no clusters. No kernel here uses TMA
+// multicast, and every TMA load reads this GPU's own memory into the issuing
+// CTA's shared memory: the kernels also run on every rank of a multi-GPU job.
+// Every mbarrier wait is bounded (about 2 s); an expired
 // wait records an error in a host-mapped status word, lets the other roles
 // time out too, waits for its own TMA loads, frees TMEM and returns.
 #include <cstdlib>
@@ -58,6 +61,8 @@ struct TcParams {
     int a_mn_major, b_mn_major;
     unsigned idesc;
     int* status;
+    long long wait_limit;  // cycles a bounded wait spins before it gives up
+    int stall;             // failure-detection test: the producer issues no loads
     DProgram epi;
     float* partials;  // column sums of the final epilogue value per 32-row group, or null
     // Split-K (single-CTA kernel only). Work items [0, full_tiles) are whole
@@ -230,13 +235,13 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             int stage = 0;
             uint32_t phase = 0;
             long long issued = 0;
-            for (int w = blockIdx.x; w < num_work && !failed; w += gridDim.x) {
+            for (int w = blockIdx.x; w < num_work && !failed && !p.stall; w += gridDim.x) {
                 int tile, split, kb0, kb1;
                 work_item(p, w, tile, split, kb0, kb1);
                 int mb, nb;
                 tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1)) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1, p.wait_limit)) {
                         failed = true;
                         break;
                     }
@@ -289,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                 const long long n = issued - 1 - i;
                 const int s = (int)(n % TSTAGES);
                 const uint32_t ph = (uint32_t)((n / TSTAGES) & 1);
-                if (!mbar_wait(full_bar(s), ph)) failed = true;
+                if (!mbar_wait(full_bar(s), ph, p.wait_limit)) failed = true;
             }
         }
     } else if (warp == 1) {
@@ -320,14 +325,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
                 }
                 const int b = t & 1;
                 const uint32_t acc_phase = (t >> 1) & 1;
-                if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
+                if (!mbar_wait(tempty_bar(b), acc_phase ^ 1, p.wait_limit)) {
                     failed = true;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * TBN);
                 for (int kb = kb0; kb < kb1; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase)) {
+                    if (!mbar_wait(full_bar(stage), phase, p.wait_limit)) {
                         failed = true;
                         break;
                     }
@@ -395,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_kernel(const __grid_con
             tile_coords(tile, p.m_blocks, p.n_blocks, mb, nb);
             const int b = t & 1;
             const uint32_t acc_phase = (t >> 1) & 1;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase, p.wait_limit));
             if (split < 0) {
                 if (!ok) {
                     failed = true;
@@ -654,13 +659,13 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
             int stage = 0;
             uint32_t phase = 0;
             long long issued = 0;
-            for (int tile = cluster_id; tile < num_tiles && !failed; tile += nclusters) {
+            for (int tile = cluster_id; tile < num_tiles && !failed && !p.stall; tile += nclusters) {
                 int mb2, nb;
                 pair_tile_coords(tile, p.m_blocks, p.n_blocks, mb2, nb);
                 const int row0 = mb2 * (2 * BM) + (int)rank * BM;
                 const int col0 = nb * P_BN + (int)rank * P_BNH;
                 for (int kb = 0; kb < p.k_blocks; ++kb) {
-                    if (!mbar_wait(empty_bar(stage), phase ^ 1)) {
+                    if (!mbar_wait(empty_bar(stage), phase ^ 1, p.wait_limit)) {
                         failed = true;
                         break;
                     }
@@ -693,7 +698,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
             const long long last = issued < P_STAGES ? issued : P_STAGES;
             for (long long i = 0; i < last; ++i) {
                 const long long n = issued - 1 - i;
-                if (!mbar_wait(full_bar((int)(n % P_STAGES)), (uint32_t)((n / P_STAGES) & 1))) failed = true;
+                if (!mbar_wait(full_bar((int)(n % P_STAGES)), (uint32_t)((n / P_STAGES) & 1), p.wait_limit)) failed = true;
             }
         }
     } else if (warp == 1 && rank == 1) {
@@ -703,7 +708,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
             uint32_t phase = 0;
             for (int tile = cluster_id; tile < num_tiles && !failed; tile += nclusters) {
                 for (int kb = 0; kb < p.k_blocks; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase)) {
+                    if (!mbar_wait(full_bar(stage), phase, p.wait_limit)) {
                         failed = true;
                         break;
                     }
@@ -729,14 +734,14 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
             for (int tile = cluster_id; tile < num_tiles && !failed; tile += nclusters, ++t) {
                 const int b = t & 1;
                 const uint32_t acc_phase = (t >> 1) & 1;
-                if (!mbar_wait(tempty_bar(b), acc_phase ^ 1)) {
+                if (!mbar_wait(tempty_bar(b), acc_phase ^ 1, p.wait_limit)) {
                     failed = true;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t d_tmem = tmem_base + (uint32_t)(b * P_BN);
                 for (int kb = 0; kb < p.k_blocks; ++kb) {
-                    if (!mbar_wait(full_bar(stage), phase)) {
+                    if (!mbar_wait(full_bar(stage), phase, p.wait_limit)) {
                         failed = true;
                         break;
                     }
@@ -768,7 +773,7 @@ __global__ void __launch_bounds__(kThreads, 1) tf32_gemm_pair_kernel(const __gri
             pair_tile_coords(tile, p.m_blocks, p.n_blocks, mb2, nb);
             const int b = t & 1;
             const uint32_t acc_phase = (t >> 1) & 1;
-            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase));
+            const bool ok = __all_sync(0xffffffffu, mbar_wait(tfull_bar(b), acc_phase, p.wait_limit));
             if (!ok) {
                 failed = true;
                 break;
@@ -901,7 +906,10 @@ bool use_pair(const ttc_gemm_desc& d, int sms) {
 }
 
 int launch_pair(TcParams& p) {
-    static int max_clusters = -1;
+    static int max_clusters_by_dev[kMaxDevices] = {};  // 0: not queried yet on that device
+    if (rt().device < 0 || rt().device >= kMaxDevices)
+        return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: device %d", rt().device);
+    int& max_clusters = max_clusters_by_dev[rt().device];
     cudaLaunchConfig_t cfg;
     std::memset(&cfg, 0, sizeof cfg);
     cudaLaunchAttribute attr[1];
@@ -914,7 +922,7 @@ int launch_pair(TcParams& p) {
     cfg.stream = rt().stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (max_clusters < 0) {
+    if (max_clusters < 1) {
         TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       P_SMEM_BYTES));
         cfg.gridDim = dim3(2 * (rt().sm_count / 2), 1, 1);
@@ -938,17 +946,12 @@ int launch_pair(TcParams& p) {
 // SM, at least 4 k-blocks (128 deep) per split, at most 16 splits. Fewer,
 // deeper splits write and re-read fewer partial tiles: the small MLP ran at
 // 34.9 us per graph replay with 4 k-blocks per split, 41.0 with 2 (3 and 8
-// measured as 4). Off with TTC_GEMM_SPLITK=0; TTC_GEMM_SPLITK_MAX and
-// TTC_GEMM_SPLITK_MINKB override the cap and the depth (read at every call,
-// for tuning sweeps).
+// measured as 4). Off with TTC_GEMM_SPLITK=0 (read at every call).
 int split_count(long long tiles, int k_blocks, int sms) {
     const char* e = getenv("TTC_GEMM_SPLITK");
     if ((e && e[0] == '0') || tiles * 2 > sms || k_blocks < 8) return 1;
     const long long fill = (sms + tiles - 1) / tiles;
-    const char* m = getenv("TTC_GEMM_SPLITK_MAX");  // tuning sweeps
-    const long long cap = m && atoi(m) >= 2 ? atoi(m) : 16;
-    const char* q = getenv("TTC_GEMM_SPLITK_MINKB");
-    const long long min_kb = q && atoi(q) >= 1 ? atoi(q) : 4;
+    constexpr long long cap = 16, min_kb = 4;
     return (int)std::max<long long>(1, std::min<long long>(std::min<long long>(fill, k_blocks / min_kb), cap));
 }
 
@@ -991,7 +994,10 @@ void launch_finalize_cols(const float* partials, int nsplit, int cols, int nseg,
 // epilogue value over the M rows, from per-32-row partial sums the epilogue
 // writes into the workspace and a fixed-order fp64 finalize.
 int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out, int mean, bool x3) {
-    static bool attr_set = false;
+    static bool attr_set_by_dev[kMaxDevices] = {};
+    if (rt().device < 0 || rt().device >= kMaxDevices)
+        return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: device %d", rt().device);
+    bool& attr_set = attr_set_by_dev[rt().device];
     if (!attr_set) {
         TTC_CUDA(cudaFuncSetAttribute(tf32_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       SMEM_BYTES));
@@ -1028,6 +1034,8 @@ int run_gemm_tf32(const ttc_gemm_desc& d, const DProgram& epi, float* reduce_out
               ((unsigned)(tn >> 3) << 17)     // N
               | ((unsigned)(tm >> 4) << 24);  // M (256 for the pair: 128 rows per CTA)
     if (int rc = device_status_ptr(&p.status)) return rc;
+    p.stall = stall_test("gemm") ? 1 : 0;
+    p.wait_limit = p.stall ? kStallTestLimitCycles : kWaitLimitCycles;
     p.epi = epi;
     const long long tiles = (long long)p.m_blocks * p.n_blocks;
     if (tiles > INT32_MAX) return set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: too many GEMM tiles");

@@ -108,6 +108,11 @@ int device_status_ptr(int** dptr) {
     return TTC_OK;
 }
 
+bool stall_test(const char* family) {
+    const char* e = getenv("TTC_TEST_STALL");
+    return e && std::strcmp(e, family) == 0;
+}
+
 // After a synchronisation: turn a recorded device-side wait expiry into an error.
 int check_device_status() {
     if (g_status_host && *(volatile int*)g_status_host) {

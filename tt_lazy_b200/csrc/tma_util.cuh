@@ -18,8 +18,17 @@ int encode_tensor_map_f32(CUtensorMap* map, const void* ptr, int rank, const uns
 // Host-mapped status word a kernel sets when one of its bounded waits expires.
 int device_status_ptr(int** dptr);
 
-#ifdef __CUDACC__
 constexpr long long kWaitLimitCycles = 4000000000ll;  // ~2 s at 1.9 GHz
+// Failure-detection test switch, read at every launch: TTC_TEST_STALL=gemm
+// (the TF32 GEMM kernels) or =chain (the TMA-staged chain kernel) makes the
+// kernel's TMA producer issue no loads at all, so nothing is ever in flight
+// and the consumers' waits run out after kStallTestLimitCycles (~1 ms); they
+// set the status word, free what they hold and return, and the next
+// synchronisation reports TTC_ERR_TIMEOUT. Returns whether `family` stalls.
+constexpr long long kStallTestLimitCycles = 2000000ll;
+bool stall_test(const char* family);
+
+#ifdef __CUDACC__
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -47,12 +56,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait for the phase with the given parity; false when it expired.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+// Bounded wait for the phase with the given parity; false when it expired
+// (after `limit` SM clock cycles).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, long long limit = kWaitLimitCycles) {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
     while (!mbar_try_wait(bar, parity))
-        if (clock64() - t0 > kWaitLimitCycles) return false;
+        if (clock64() - t0 > limit) return false;
     return true;
 }
 

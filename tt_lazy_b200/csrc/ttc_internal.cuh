@@ -35,6 +35,11 @@ struct Runtime {
     unsigned next_ticket = 0;
 };
 Runtime& rt();
+// One-time per-device set-up (kernel attributes, occupancy, loaded modules)
+// is cached in arrays indexed by the device ordinal: function attributes and
+// modules belong to a device's context, so a ttc_shutdown / ttc_init on
+// another device must not reuse the first device's.
+constexpr int kMaxDevices = 64;
 // Scratch of at least `bytes`, valid until the next call that asks for more.
 int workspace(size_t bytes, void** out);
 inline void count_launch(unsigned n = 1) { rt().kernels += n; }
