@@ -319,8 +319,12 @@ int ttc_gemm_select_path(const ttc_gemm_desc* desc);
  * slice of the batch; the only exchange is the sum of per-shard partial
  * reductions. NCCL communicator, created non-blocking; every wait is bounded
  * by timeout_ms and an expired wait aborts the communicator and returns
- * TTC_ERR_TIMEOUT instead of hanging. No reference counterpart (the
- * reference is single-process). */
+ * TTC_ERR_TIMEOUT instead of hanging. ttc_allreduce_sum enqueues the
+ * collective on the library stream and returns without waiting for it; the
+ * next synchronisation (ttc_synchronize, a ttc_memcpy_d2h, the next
+ * ttc_allreduce_sum, ttc_comm_destroy) polls for its completion against the
+ * deadline and the communicator's asynchronous error, and reports a failure
+ * there. No reference counterpart (the reference is single-process). */
 #define TTC_UNIQUE_ID_BYTES 128
 int ttc_comm_unique_id(uint8_t out[TTC_UNIQUE_ID_BYTES]);
 int ttc_comm_init(int nranks, int rank, const uint8_t id[TTC_UNIQUE_ID_BYTES], int timeout_ms);

@@ -1,14 +1,22 @@
 // comm.cpp -- the one collective of row-sharded data parallelism: the sum of
 // per-shard partial reductions across ranks (one process per GPU).
 //
-// NCCL communicator created non-blocking (ncclConfig_t.blocking = 0). Every
-// wait -- communicator set-up, enqueue, completion on the stream -- polls
-// against a host deadline; an expired deadline aborts the communicator and
-// returns TTC_ERR_TIMEOUT, so a rank that died or never joined turns into an
-// error status instead of a hang. No reference counterpart: the reference is
+// NCCL communicator created non-blocking (ncclConfig_t.blocking = 0).
+// ttc_allreduce_sum enqueues the collective on the library stream and
+// returns once NCCL has accepted it: the host does not wait for it, so the
+// next step's work is enqueued while this step's collective runs. Every wait
+// polls against a host deadline -- communicator set-up, enqueue, and the
+// completion of an outstanding collective, which the library's
+// synchronisation points (sync_stream_bounded: ttc_synchronize, device ->
+// host copies, the next all-reduce's enqueue check) poll for instead of
+// blocking in cudaStreamSynchronize. An expired deadline or an asynchronous
+// NCCL error aborts the communicator and returns TTC_ERR_TIMEOUT /
+// TTC_ERR_NCCL, so a rank that died or never joined turns into an error
+// status instead of a hang. No reference counterpart: the reference is
 // single-process and has no collectives.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <chrono>
 #include <cstdlib>
 #include <cstring>
@@ -18,6 +26,7 @@
 
 namespace ttc {
 int set_error(int code, const char* fmt, ...);
+int sync_stream_bounded(cudaStream_t st);
 }
 
 namespace {
@@ -38,6 +47,18 @@ ncclComm_t g_comm = nullptr;
 
 using Clock = std::chrono::steady_clock;
 
+// An all-reduce enqueued and not yet seen complete, and the host deadline of
+// the latest one (its enqueue time + its timeout).
+std::atomic<bool> g_outstanding{false};
+Clock::time_point g_deadline;
+int g_timeout_ms = 0;
+
+void abort_comm() {
+    ncclCommAbort(g_comm);
+    g_comm = nullptr;
+    g_outstanding = false;
+}
+
 // Polls the communicator's async state until it leaves ncclInProgress.
 int wait_comm(int timeout_ms, const char* what) {
     const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
@@ -47,13 +68,11 @@ int wait_comm(int timeout_ms, const char* what) {
         if (r != ncclSuccess) st = r;
         if (st == ncclSuccess) return TTC_OK;
         if (st != ncclInProgress) {
-            ncclCommAbort(g_comm);
-            g_comm = nullptr;
+            abort_comm();
             return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: %s failed: %s", what, ncclGetErrorString(st));
         }
         if (Clock::now() > deadline) {
-            ncclCommAbort(g_comm);
-            g_comm = nullptr;
+            abort_comm();
             return ttc::set_error(TTC_ERR_TIMEOUT, "tt_cuda: %s did not complete within %d ms; communicator aborted",
                                   what, timeout_ms);
         }
@@ -95,41 +114,40 @@ int ttc_allreduce_sum(float* buf, size_t count, int timeout_ms) {
     if (inject_fault("allreduce")) return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: injected all-reduce fault");
     if (!g_comm) return ttc::set_error(TTC_ERR_NOT_INITIALIZED, "tt_cuda: ttc_comm_init() not called");
     if (!buf && count) return ttc::set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: allreduce buffer is NULL");
+    if (timeout_ms <= 0) return ttc::set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: all-reduce timeout %d ms", timeout_ms);
+    // an earlier collective that failed asynchronously is reported here,
+    // before another one is queued behind it
+    ncclResult_t async = ncclSuccess;
+    ncclCommGetAsyncError(g_comm, &async);
+    if (async != ncclSuccess && async != ncclInProgress) {
+        abort_comm();
+        return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: an earlier all-reduce failed: %s", ncclGetErrorString(async));
+    }
+    if (g_outstanding && Clock::now() > g_deadline && cudaStreamQuery((cudaStream_t)ttc_get_stream()) == cudaErrorNotReady) {
+        abort_comm();
+        return ttc::set_error(TTC_ERR_TIMEOUT, "tt_cuda: an earlier all-reduce did not complete within %d ms; aborted",
+                              g_timeout_ms);
+    }
     cudaStream_t st = (cudaStream_t)ttc_get_stream();
     ncclResult_t r = ncclAllReduce(buf, buf, count, ncclFloat32, ncclSum, g_comm, st);
     if (r != ncclSuccess && r != ncclInProgress) {
-        ncclCommAbort(g_comm);
-        g_comm = nullptr;
+        abort_comm();
         return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: ncclAllReduce: %s", ncclGetErrorString(r));
     }
     if (int rc = wait_comm(timeout_ms, "all-reduce enqueue")) return rc;
-    // Completion on the stream, bounded by the same deadline.
-    const auto deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
-    for (;;) {
-        cudaError_t e = cudaStreamQuery(st);
-        if (e == cudaSuccess) break;
-        if (e != cudaErrorNotReady)
-            return ttc::set_error(TTC_ERR_CUDA, "tt_cuda: all-reduce stream: %s", cudaGetErrorString(e));
-        ncclResult_t async = ncclSuccess;
-        ncclCommGetAsyncError(g_comm, &async);
-        if (async != ncclSuccess && async != ncclInProgress) {
-            ncclCommAbort(g_comm);
-            g_comm = nullptr;
-            return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: all-reduce failed: %s", ncclGetErrorString(async));
-        }
-        if (Clock::now() > deadline) {
-            ncclCommAbort(g_comm);
-            g_comm = nullptr;
-            return ttc::set_error(TTC_ERR_TIMEOUT, "tt_cuda: all-reduce did not complete within %d ms; aborted",
-                                  timeout_ms);
-        }
-        std::this_thread::sleep_for(std::chrono::microseconds(20));
-    }
+    // Not waited for here: the next synchronisation point polls for it
+    // against this deadline (sync_stream_bounded).
+    g_timeout_ms = timeout_ms;
+    g_deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
+    g_outstanding = true;
     return TTC_OK;
 }
 
 int ttc_comm_destroy(void) {
     if (!g_comm) return TTC_OK;
+    if (g_outstanding) {  // a collective still queued: let it finish first (bounded)
+        if (ttc::sync_stream_bounded((cudaStream_t)ttc_get_stream()) != TTC_OK) return TTC_OK;  // aborted
+    }
     ncclResult_t r = ncclCommFinalize(g_comm);
     if (r == ncclSuccess || r == ncclInProgress) {
         const auto deadline = Clock::now() + std::chrono::milliseconds(10000);
@@ -144,12 +162,47 @@ int ttc_comm_destroy(void) {
             return TTC_OK;
         }
     }
-    ncclCommAbort(g_comm);
-    g_comm = nullptr;
+    abort_comm();
     return TTC_OK;
 }
 
 }  // extern "C"
+
+namespace ttc {
+// Waits for the work queued on `st`. With an all-reduce outstanding the wait
+// polls against its host deadline and the communicator's asynchronous error
+// (a peer that died leaves the collective spinning on this GPU; the abort
+// releases it) instead of blocking in cudaStreamSynchronize.
+int sync_stream_bounded(cudaStream_t st) {
+    if (g_comm && g_outstanding) {
+        for (;;) {
+            const cudaError_t e = cudaStreamQuery(st);
+            if (e == cudaSuccess) {
+                g_outstanding = false;
+                return TTC_OK;
+            }
+            if (e != cudaErrorNotReady)
+                return set_error(TTC_ERR_CUDA, "tt_cuda: stream with an all-reduce: %s", cudaGetErrorString(e));
+            ncclResult_t async = ncclSuccess;
+            ncclCommGetAsyncError(g_comm, &async);
+            if (async != ncclSuccess && async != ncclInProgress) {
+                abort_comm();
+                return set_error(TTC_ERR_NCCL, "tt_cuda: all-reduce failed: %s", ncclGetErrorString(async));
+            }
+            if (Clock::now() > g_deadline) {
+                abort_comm();
+                return set_error(TTC_ERR_TIMEOUT, "tt_cuda: all-reduce did not complete within %d ms; aborted",
+                                 g_timeout_ms);
+            }
+            std::this_thread::sleep_for(std::chrono::microseconds(20));
+        }
+    }
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+        return set_error(TTC_ERR_CUDA, "tt_cuda: cudaStreamSynchronize failed: %s", cudaGetErrorString(e));
+    return TTC_OK;
+}
+}  // namespace ttc
 
 #else  // built without NCCL headers
 
@@ -161,4 +214,12 @@ int ttc_comm_init(int, int, const uint8_t*, int) {
 int ttc_allreduce_sum(float*, size_t, int) { return ttc::set_error(TTC_ERR_UNSUPPORTED, "tt_cuda: built without NCCL"); }
 int ttc_comm_destroy(void) { return TTC_OK; }
 }
+namespace ttc {
+int sync_stream_bounded(cudaStream_t st) {
+    const cudaError_t e = cudaStreamSynchronize(st);
+    if (e != cudaSuccess)
+        return set_error(TTC_ERR_CUDA, "tt_cuda: cudaStreamSynchronize failed: %s", cudaGetErrorString(e));
+    return TTC_OK;
+}
+}  // namespace ttc
 #endif

@@ -298,7 +298,7 @@ int ttc_init(int device) {
 int ttc_shutdown(void) {
     Runtime& r = rt();
     if (!r.initialized) return TTC_OK;
-    cudaStreamSynchronize(r.stream);
+    sync_stream_bounded(r.stream);  // an outstanding all-reduce is waited for against its deadline
     if (r.copy_stream) {
         cudaStreamSynchronize(r.copy_stream);
         for (auto& e : r.tickets)
@@ -326,7 +326,7 @@ int ttc_set_stream(void* s) {
 
 int ttc_synchronize(void) {
     TTC_REQUIRE_INIT();
-    TTC_CUDA(cudaStreamSynchronize(rt().stream));
+    if (int rc = sync_stream_bounded(rt().stream)) return rc;
     return check_device_status();
 }
 
@@ -432,6 +432,9 @@ int ttc_timer_elapsed(int from, int to, float* ms) {
     TTC_REQUIRE_INIT();
     if (!ms || from < 0 || to < 0 || from >= 4096 || to >= 4096 || !g_marks[from] || !g_marks[to])
         return set_error(TTC_ERR_INVALID_ARGUMENT, "tt_cuda: timer_elapsed: unknown mark");
+    if (cudaEventQuery(g_marks[to]) != cudaSuccess) {
+        if (int rc = sync_stream_bounded(rt().stream)) return rc;  // bounded when an all-reduce is queued
+    }
     TTC_CUDA(cudaEventSynchronize(g_marks[to]));
     TTC_CUDA(cudaEventElapsedTime(ms, g_marks[from], g_marks[to]));
     return TTC_OK;
@@ -473,7 +476,7 @@ int ttc_memcpy_d2h(void* dst, const void* src, size_t bytes) {
     TTC_REQUIRE_INIT();
     if (bytes == 0) return TTC_OK;
     TTC_CUDA(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, rt().stream));
-    TTC_CUDA(cudaStreamSynchronize(rt().stream));
+    if (int rc = sync_stream_bounded(rt().stream)) return rc;
     return check_device_status();
 }
 

@@ -35,6 +35,9 @@ struct Runtime {
     unsigned next_ticket = 0;
 };
 Runtime& rt();
+// Waits for the work queued on `st`; with an all-reduce outstanding, polls
+// against its deadline instead of blocking (comm.cpp).
+int sync_stream_bounded(cudaStream_t st);
 // One-time per-device set-up (kernel attributes, occupancy, loaded modules)
 // is cached in arrays indexed by the device ordinal: function attributes and
 // modules belong to a device's context, so a ttc_shutdown / ttc_init on

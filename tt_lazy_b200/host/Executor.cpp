@@ -324,6 +324,10 @@ void TapeExecutor::execute_tape(Tape& tape) {
     std::set<std::pair<NodeId, uint16_t>> keep;
     for (const auto& t : tape.outputs())
         if (t.is_lazy()) keep.insert({t.producer_node(), t.output_index()});
+    // an op's own handle on its first output (TapeOperation::result) is dropped
+    // with the executor's, so a released result goes back to the pool at once
+    std::map<NodeId, TapeOperation*> producer;
+    for (const auto& op : ops) producer[op->node_id] = op.get();
     for (size_t i = 0; i < ops.size(); ++i) {
         if (prof) {
             labels.push_back(tt_lazy::op_label(*ops[i]));
@@ -345,7 +349,12 @@ void TapeExecutor::execute_tape(Tape& tape) {
         for (const auto& o : ops[i]->operands) {
             if (!o.lazy) continue;
             const auto key = std::make_pair(o.node, o.index);
-            if (last_use[key] == i && !keep.count(key)) results_.erase(key);
+            if (last_use[key] != i || keep.count(key)) continue;
+            results_.erase(key);
+            if (key.second == 0) {
+                auto p = producer.find(key.first);
+                if (p != producer.end()) p->second->result.reset();
+            }
         }
     }
     if (prof) {
@@ -1262,7 +1271,9 @@ void CompiledTape::capture() {
     if (graph_) return;
     for (const auto& op : tape_->operations())
         if (op->op_type == AllReduceArgs::type_id())
-            throw std::runtime_error("Plan.capture: a plan with an all-reduce is not captured (it waits on the host)");
+            throw std::runtime_error(
+                "Plan.capture: a plan with an all-reduce is not captured (its completion is checked on the host "
+                "against the communicator's deadline, which a graph replay would bypass)");
     run();  // warm: specialised kernels compiled, scratch grown, buffer pool filled
     check(ttc_synchronize());
     auto& mm = MemoryManager::instance();
