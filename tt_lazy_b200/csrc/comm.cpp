@@ -47,9 +47,11 @@ ncclComm_t g_comm = nullptr;
 
 using Clock = std::chrono::steady_clock;
 
-// An all-reduce enqueued and not yet seen complete, and the host deadline of
-// the latest one (its enqueue time + its timeout).
+// An all-reduce enqueued and not yet seen complete: an event recorded right
+// after the latest one (completions are in stream order, so it covers the
+// earlier ones) and its host deadline (its enqueue time + its timeout).
 std::atomic<bool> g_outstanding{false};
+cudaEvent_t g_done = nullptr;
 Clock::time_point g_deadline;
 int g_timeout_ms = 0;
 
@@ -57,6 +59,34 @@ void abort_comm() {
     ncclCommAbort(g_comm);
     g_comm = nullptr;
     g_outstanding = false;
+}
+
+// Polls the latest all-reduce's completion against its deadline and the
+// communicator's asynchronous error. TTC_OK once it completed (or when none
+// is outstanding).
+int wait_outstanding() {
+    while (g_comm && g_outstanding) {
+        const cudaError_t e = cudaEventQuery(g_done);
+        if (e == cudaSuccess) {
+            g_outstanding = false;
+            return TTC_OK;
+        }
+        if (e != cudaErrorNotReady)
+            return ttc::set_error(TTC_ERR_CUDA, "tt_cuda: all-reduce completion: %s", cudaGetErrorString(e));
+        ncclResult_t async = ncclSuccess;
+        ncclCommGetAsyncError(g_comm, &async);
+        if (async != ncclSuccess && async != ncclInProgress) {
+            abort_comm();
+            return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: all-reduce failed: %s", ncclGetErrorString(async));
+        }
+        if (Clock::now() > g_deadline) {
+            abort_comm();
+            return ttc::set_error(TTC_ERR_TIMEOUT, "tt_cuda: all-reduce did not complete within %d ms; aborted",
+                                  g_timeout_ms);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+    return TTC_OK;
 }
 
 // Polls the communicator's async state until it leaves ncclInProgress.
@@ -107,7 +137,12 @@ int ttc_comm_init(int nranks, int rank, const uint8_t id[TTC_UNIQUE_ID_BYTES], i
         g_comm = nullptr;
         return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: ncclCommInitRankConfig: %s", ncclGetErrorString(r));
     }
-    return wait_comm(timeout_ms, "communicator initialisation");
+    if (int rc = wait_comm(timeout_ms, "communicator initialisation")) return rc;
+    if (!g_done && cudaEventCreateWithFlags(&g_done, cudaEventDisableTiming) != cudaSuccess) {
+        abort_comm();
+        return ttc::set_error(TTC_ERR_CUDA, "tt_cuda: all-reduce completion event could not be created");
+    }
+    return TTC_OK;
 }
 
 int ttc_allreduce_sum(float* buf, size_t count, int timeout_ms) {
@@ -123,7 +158,7 @@ int ttc_allreduce_sum(float* buf, size_t count, int timeout_ms) {
         abort_comm();
         return ttc::set_error(TTC_ERR_NCCL, "tt_cuda: an earlier all-reduce failed: %s", ncclGetErrorString(async));
     }
-    if (g_outstanding && Clock::now() > g_deadline && cudaStreamQuery((cudaStream_t)ttc_get_stream()) == cudaErrorNotReady) {
+    if (g_outstanding && cudaEventQuery(g_done) == cudaErrorNotReady && Clock::now() > g_deadline) {
         abort_comm();
         return ttc::set_error(TTC_ERR_TIMEOUT, "tt_cuda: an earlier all-reduce did not complete within %d ms; aborted",
                               g_timeout_ms);
@@ -137,6 +172,10 @@ int ttc_allreduce_sum(float* buf, size_t count, int timeout_ms) {
     if (int rc = wait_comm(timeout_ms, "all-reduce enqueue")) return rc;
     // Not waited for here: the next synchronisation point polls for it
     // against this deadline (sync_stream_bounded).
+    if (cudaEventRecord(g_done, st) != cudaSuccess) {
+        abort_comm();
+        return ttc::set_error(TTC_ERR_CUDA, "tt_cuda: all-reduce completion event record failed");
+    }
     g_timeout_ms = timeout_ms;
     g_deadline = Clock::now() + std::chrono::milliseconds(timeout_ms);
     g_outstanding = true;
@@ -145,9 +184,7 @@ int ttc_allreduce_sum(float* buf, size_t count, int timeout_ms) {
 
 int ttc_comm_destroy(void) {
     if (!g_comm) return TTC_OK;
-    if (g_outstanding) {  // a collective still queued: let it finish first (bounded)
-        if (ttc::sync_stream_bounded((cudaStream_t)ttc_get_stream()) != TTC_OK) return TTC_OK;  // aborted
-    }
+    if (wait_outstanding() != TTC_OK) return TTC_OK;  // a queued collective that never finished: aborted
     ncclResult_t r = ncclCommFinalize(g_comm);
     if (r == ncclSuccess || r == ncclInProgress) {
         const auto deadline = Clock::now() + std::chrono::milliseconds(10000);
@@ -169,34 +206,13 @@ int ttc_comm_destroy(void) {
 }  // extern "C"
 
 namespace ttc {
-// Waits for the work queued on `st`. With an all-reduce outstanding the wait
-// polls against its host deadline and the communicator's asynchronous error
-// (a peer that died leaves the collective spinning on this GPU; the abort
-// releases it) instead of blocking in cudaStreamSynchronize.
+// Waits for the work queued on `st`. An outstanding all-reduce is waited for
+// first, by polling its completion event against its host deadline and the
+// communicator's asynchronous error (a peer that died leaves the collective
+// spinning on this GPU; the abort releases it); everything else on the stream
+// then finishes on its own.
 int sync_stream_bounded(cudaStream_t st) {
-    if (g_comm && g_outstanding) {
-        for (;;) {
-            const cudaError_t e = cudaStreamQuery(st);
-            if (e == cudaSuccess) {
-                g_outstanding = false;
-                return TTC_OK;
-            }
-            if (e != cudaErrorNotReady)
-                return set_error(TTC_ERR_CUDA, "tt_cuda: stream with an all-reduce: %s", cudaGetErrorString(e));
-            ncclResult_t async = ncclSuccess;
-            ncclCommGetAsyncError(g_comm, &async);
-            if (async != ncclSuccess && async != ncclInProgress) {
-                abort_comm();
-                return set_error(TTC_ERR_NCCL, "tt_cuda: all-reduce failed: %s", ncclGetErrorString(async));
-            }
-            if (Clock::now() > g_deadline) {
-                abort_comm();
-                return set_error(TTC_ERR_TIMEOUT, "tt_cuda: all-reduce did not complete within %d ms; aborted",
-                                 g_timeout_ms);
-            }
-            std::this_thread::sleep_for(std::chrono::microseconds(20));
-        }
-    }
+    if (int rc = wait_outstanding()) return rc;  // the only work here that can wait on another rank
     const cudaError_t e = cudaStreamSynchronize(st);
     if (e != cudaSuccess)
         return set_error(TTC_ERR_CUDA, "tt_cuda: cudaStreamSynchronize failed: %s", cudaGetErrorString(e));
