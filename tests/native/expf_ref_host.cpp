@@ -6,8 +6,10 @@
 // intrinsic below is one correctly rounded operation, as on the device.
 //
 // usage: expf_ref_host STRIDE -> prints
-//   "n=<count> exp_mismatch=<m> sig_mismatch=<s> sig_over1ulp=<k> fma_variant=<0|1>"
-// over every STRIDE-th 32-bit pattern (NaN results compare equal to NaN).
+//   "n=<count> exp_mismatch=<m> fast_mismatch=<f> sig_mismatch=<s> sig_over1ulp=<k> fma_variant=<0|1>"
+// over every STRIDE-th 32-bit pattern (NaN results compare equal to NaN);
+// fast_mismatch counts the inputs with |x| <= 87 where expf_ref_fast (the
+// kernels' rearranged form) differs from expf.
 // fma_variant reports whether this libm's expf is glibc's FMA build (the one
 // the header restates) at the input where its two x86-64 builds differ.
 #include <cmath>
@@ -65,12 +67,14 @@ int main(int argc, char** argv) {
     const long long stride = argc > 1 ? std::atoll(argv[1]) : 1;
     ExpTable tab;
     exp_table_init(tab);  // one "thread" of a one-thread block fills every entry
-    long long n = 0, exp_bad = 0, sig_bad = 0, sig_far = 0;
-#pragma omp parallel for reduction(+ : n, exp_bad, sig_bad, sig_far) schedule(dynamic, 1 << 16)
+    long long n = 0, exp_bad = 0, fast_bad = 0, sig_bad = 0, sig_far = 0;
+#pragma omp parallel for reduction(+ : n, exp_bad, fast_bad, sig_bad, sig_far) schedule(dynamic, 1 << 16)
     for (long long u = 0; u < (1ll << 32); u += stride) {
         const float x = __int_as_float((int)(unsigned)u);
         ++n;
-        exp_bad += !same(expf_ref(x, tab), ::expf(x));
+        const float ex = ::expf(x);
+        exp_bad += !same(expf_ref(x, tab), ex);
+        if (fabsf(x) <= 87.0f) fast_bad += !same(expf_ref_fast(x, tab), ex);
         const float want = 1.0f / (1.0f + ::expf(-x));
         const float got = sigmoid_ref(x, tab);
         if (!same(got, want)) {
@@ -81,7 +85,7 @@ int main(int argc, char** argv) {
     }
     volatile float probe = 0x1.04845ep+5f;  // volatile: no compile-time folding of expf
     const int fma_variant = __float_as_int(::expf(probe)) == __float_as_int(0x1.f93e38p+46f);
-    std::printf("n=%lld exp_mismatch=%lld sig_mismatch=%lld sig_over1ulp=%lld fma_variant=%d\n", n, exp_bad, sig_bad,
-                sig_far, fma_variant);
+    std::printf("n=%lld exp_mismatch=%lld fast_mismatch=%lld sig_mismatch=%lld sig_over1ulp=%lld fma_variant=%d\n", n,
+                exp_bad, fast_bad, sig_bad, sig_far, fma_variant);
     return 0;
 }
