@@ -1,3 +1,5 @@
-// TapeEvaluationManager.hpp -- forwarding header: the declarations live in TapeExecutor.hpp / Tape.hpp.
+// TapeEvaluationManager.hpp -- the reference's include name for TapeEvaluationManager (src/*/TapeEvaluationManager.hpp there), so
+// code written against the reference's headers compiles against this front end
+// unchanged; the declarations live in TapeExecutor.hpp / Tape.hpp.
 #pragma once
 #include "TapeExecutor.hpp"

@@ -1,3 +1,5 @@
-// TapeOperation.hpp -- forwarding header: the declarations live in TapeExecutor.hpp / Tape.hpp.
+// TapeOperation.hpp -- the reference's include name for TapeOperation (src/*/TapeOperation.hpp there), so
+// code written against the reference's headers compiles against this front end
+// unchanged; the declarations live in TapeExecutor.hpp / Tape.hpp.
 #pragma once
 #include "TapeExecutor.hpp"
