@@ -1,4 +1,4 @@
-// MemoryManager.hpp -- the reference's include name for MemoryManager (src/*/MemoryManager.hpp there), so
+// MemoryManager.hpp -- the reference's include name for MemoryManager (src/core/MemoryManager.hpp there), so
 // code written against the reference's headers compiles against this front end
 // unchanged; the declarations live in TapeExecutor.hpp / Tape.hpp.
 #pragma once

@@ -1,4 +1,4 @@
-// TapeEvaluationManager.hpp -- the reference's include name for TapeEvaluationManager (src/*/TapeEvaluationManager.hpp there), so
+// TapeEvaluationManager.hpp -- the reference's include name for TapeEvaluationManager (src/tape/TapeEvaluationManager.hpp there), so
 // code written against the reference's headers compiles against this front end
 // unchanged; the declarations live in TapeExecutor.hpp / Tape.hpp.
 #pragma once

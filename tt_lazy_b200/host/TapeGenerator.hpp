@@ -1,4 +1,4 @@
-// TapeGenerator.hpp -- the reference's include name for TapeGenerator (src/*/TapeGenerator.hpp there), so
+// TapeGenerator.hpp -- the reference's include name for TapeGenerator (src/tape/TapeGenerator.hpp there), so
 // code written against the reference's headers compiles against this front end
 // unchanged; the declarations live in TapeExecutor.hpp / Tape.hpp.
 #pragma once

@@ -1,4 +1,4 @@
-// TapeOperation.hpp -- the reference's include name for TapeOperation (src/*/TapeOperation.hpp there), so
+// TapeOperation.hpp -- the reference's include name for TapeOperation (src/tape/TapeOperation.hpp there), so
 // code written against the reference's headers compiles against this front end
 // unchanged; the declarations live in TapeExecutor.hpp / Tape.hpp.
 #pragma once
